@@ -1,0 +1,407 @@
+"""Benchmark: Q8-KV decode attention at 32K context (8 full-attention layers).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload (per GPU): one sequence whose 8 full-attention layers each hold a
+distinct Q8 cache of 32768 tokens (32512 packed + 256 exact residual; the
+reference-reachable state), 16 query heads / 4 KV heads x 256, bf16.  K and V
+are seeded N(0,1) with 1% of channels per KV head scaled x8.  One step =
+for each layer: append the new token (residual), decode attention over the
+whole cache, compact (one 128-token block is quantized into the banks every
+128 steps).  Every 128 steps the cache is rolled back to its starting state
+(reference swap, no device work) so the context stays at 32768..32895.
+
+Reported: ``value`` = tokens/s through the 8 attention layers summed over all
+GPUs, device-timed with CUDA events (inputs resident in HBM; the 8 caches,
+591 MB, exceed L2); ``e2e`` = the same through the public API with the step's
+inputs copied from pinned host memory and outputs read back every step;
+``roofline`` = achieved HBM GB/s of the decode kernel (algorithmic bytes per
+launch / mean launch time) against the measured copy bandwidth;
+``cpu_baseline`` = the reference's PyTorch CPU path (restated in
+``oracle/ckv_cpu_path.py``) on this host.  With N > 1 every rank runs its own
+sequence (weak scaling: sequences are independent, no collective on the data
+path).  ``--impl reference`` times that CPU path alone.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = ('Q8-KV decode attn µs/step & HBM GB/s (% peak) at 32K ctx; '
+          '1/2/4/8-GPU tok/s')
+HQ, HKV, D, LAYERS, CONTEXT, BITS = 16, 4, 256, 8, 32768, 8
+SCALE = 1 / 16
+ROLLBACK = 128
+
+
+def peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+def init_dist():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device('cuda', local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device='cuda', dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device: int):
+        self.device, self.proc = device, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '20', '-i', str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'samples': 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return {'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Workload
+# ---------------------------------------------------------------------------
+def synthetic_kv(gen, length, device):
+    """K, V ~ N(0,1) bf16 with 1% of channels per KV head scaled x8."""
+    k = torch.randn(1, HKV, length, D, generator=gen, device=device, dtype=torch.float32)
+    v = torch.randn(1, HKV, length, D, generator=gen, device=device, dtype=torch.float32)
+    count = -(-D // 100)
+    for h in range(HKV):
+        idx = torch.randperm(D, generator=gen, device=device)[:count]
+        k[:, h, :, idx] *= 8
+        v[:, h, :, idx] *= 8
+    return k.bfloat16(), v.bfloat16()
+
+
+def algorithmic_bytes(view) -> int:
+    """Codes + meta of every packed token, the exact residual, q and output."""
+    packed, resid = view.packed_tokens, view.keys.shape[2]
+    per_token = 2 * D * BITS // 8 + D * 8 // 128 + (D // 64) * 8      # 560 at Q8, D=256
+    return HKV * (packed * per_token + resid * 2 * D * 2) + 2 * HQ * D * 2
+
+
+class Sequence:
+    """8 layer caches of one sequence plus per-step inputs."""
+
+    def __init__(self, seed, steps, device):
+        from trpg_b200.quantized_kv import QuantizedAttentionLayer
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.layers = []
+        with torch.inference_mode():
+            for _ in range(LAYERS):
+                k, v = synthetic_kv(gen, CONTEXT - 1, device)
+                layer = QuantizedAttentionLayer(BITS)
+                layer.update(k, v)
+                del k, v
+                self.layers.append(layer)
+        torch.cuda.synchronize()
+        n = min(steps, ROLLBACK)
+        self.q = torch.randn(n, LAYERS, 1, HQ, 1, D, generator=gen, device=device).bfloat16()
+        self.kn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
+        self.vn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
+        self.snap = [self._snapshot(l) for l in self.layers]
+
+    @staticmethod
+    def _snapshot(layer):
+        kb, vb = layer.key_bank, layer.value_bank
+        return (layer.keys, layer.values, layer.cumulative_length, kb.data, kb.meta, kb.units,
+                vb.data, vb.meta, vb.units)
+
+    def rollback(self):
+        for layer, s in zip(self.layers, self.snap):
+            (layer.keys, layer.values, layer.cumulative_length, layer.key_bank.data,
+             layer.key_bank.meta, layer.key_bank.units, layer.value_bank.data,
+             layer.value_bank.meta, layer.value_bank.units) = s
+
+
+def run_steps(seq, decode, steps, start=0, outs=None):
+    """Run ``steps`` decode steps (all layers); returns #kernel launches."""
+    launches = 0
+    for s in range(start, start + steps):
+        i = s % ROLLBACK
+        if i == 0 and s:
+            seq.rollback()
+        for li, layer in enumerate(seq.layers):
+            view = layer.append_for_attention(seq.kn[i, li], seq.vn[i, li])
+            out = decode(seq.q[i, li], view, SCALE)
+            launches += 1
+            units = layer.key_bank.units
+            layer.compact_residual()
+            launches += layer.key_bank.units != units
+            if outs is not None:
+                outs[li] = out
+    return launches
+
+
+def time_kernel(seq, decode, launches=64):
+    """Mean device time of one decode launch, on its own stream, queue pre-filled."""
+    times, sizes = [], []
+    torch.cuda.synchronize()
+    pairs = []
+    torch.cuda._sleep(int(2e7))   # keep the GPU busy while launches are enqueued
+    for s in range(launches):
+        layer = seq.layers[s % LAYERS]
+        view = layer.append_for_attention(seq.kn[0, s % LAYERS], seq.vn[0, s % LAYERS])
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        decode(seq.q[0, s % LAYERS], view, SCALE)
+        b.record()
+        pairs.append((a, b))
+        sizes.append(algorithmic_bytes(view))
+        # undo the append without device work
+        layer.keys, layer.values = layer.keys[:, :, :-1], layer.values[:, :, :-1]
+        layer.cumulative_length -= 1
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in pairs]
+    seq.rollback()
+    return statistics.mean(times) * 1e-3, statistics.mean(sizes)
+
+
+def cpu_reference(steps, warmup, sample_layers=1):
+    """The reference CPU path on one layer per step (a bounded sample)."""
+    from oracle import ckv_cpu_path as P
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(12)
+    layer = P.CpuLayer(BITS)
+    k, v = synthetic_kv(gen, CONTEXT - 1, 'cpu')
+    layer.update(k, v)
+    del k, v
+    snap = (layer.keys, layer.values, layer.length, layer.kd, layer.km, layer.vd, layer.vm)
+    q = torch.randn(1, HQ, 1, D, generator=gen).bfloat16()
+    kn = torch.randn(1, HKV, 1, D, generator=gen).bfloat16()
+    for i in range(warmup):
+        P.decode_step(layer, q, kn, kn, SCALE)
+    times = []
+    for i in range(steps):
+        if i and i % ROLLBACK == 0:
+            layer.keys, layer.values, layer.length, layer.kd, layer.km, layer.vd, layer.vm = snap
+        t = time.perf_counter()
+        P.decode_step(layer, q, kn, kn, SCALE)
+        times.append(time.perf_counter() - t)
+    per_layer = statistics.mean(times)
+    return {'value': 1.0 / (LAYERS * per_layer), 'unit': 'tok/s', 'cores': threads,
+            'kind': 'port', 'ms_per_layer': per_layer * 1e3,
+            'sample': f'{steps} decode steps of 1 of the 8 identical 32K-token Q8 layers '
+                      f'(append + dequantize + SDPA + compact), torch CPU ops, {threads} threads; '
+                      f'tok/s = 1 / (8 x mean layer time)'}
+
+
+# ---------------------------------------------------------------------------
+# Arms
+# ---------------------------------------------------------------------------
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    base = cpu_reference(args.steps, args.warmup)
+    line = {'impl': 'reference', 'metric': METRIC, 'value': base['value'], 'unit': 'tok/s',
+            'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': base['ms_per_layer'] * LAYERS, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'u8/bf16', 'data': 'synthetic',
+            'config': config(args, world),
+            'cpu_baseline': {k: base[k] for k in ('value', 'unit', 'cores', 'kind', 'sample')},
+            'e2e': {'value': base['value'], 'unit': 'tok/s', 'h2d_bytes_per_step': 0,
+                    'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config(args, world):
+    return {'workload': 'single-sequence Q8 decode, 8 layers x 32K context (32512 packed + 256 '
+                        'bf16 recent), 16q/4kv x 256, append-quantize + decode per layer',
+            'model': 'attention only (no weights)', 'global_batch': world, 'seq_len': CONTEXT,
+            'parallelism': f'dp{world} (independent sequences)', 'layers': LAYERS,
+            'heads_q': HQ, 'heads_kv': HKV, 'head_dim': D, 'bits': BITS,
+            'l2': 'inputs larger than L2 (8 distinct caches, 591 MB per GPU)'}
+
+
+def b200_arm(args, world, rank, local):
+    from trpg_b200 import _native
+    from trpg_b200.compressed_kv_kernels import decode
+    _native.load()
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    seq = Sequence(1000 + rank, args.steps + args.warmup, device)
+    # untimed warm-up
+    run_steps(seq, decode, args.warmup)
+    seq.rollback()
+    torch.cuda.synchronize()
+
+    # ---- device-timed region ------------------------------------------------
+    clocks = Clocks(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    launches = run_steps(seq, decode, args.steps)
+    stop.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    seq.rollback()
+
+    # ---- end to end through the public API with host buffers -----------------
+    pin = lambda t: t.cpu().pin_memory()
+    hq, hk, hv = pin(seq.q), pin(seq.kn), pin(seq.vn)
+    host_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
+    from trpg_b200.compressed_kv_attention import compressed_kv_decode
+    outs = [None] * LAYERS
+    e2e_steps = args.steps
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for s in range(e2e_steps):
+        i = s % ROLLBACK
+        if i == 0 and s:
+            seq.rollback()
+        q = hq[i].to(device, non_blocking=True)
+        kn = hk[i].to(device, non_blocking=True)
+        vn = hv[i].to(device, non_blocking=True)
+        with torch.inference_mode():
+            for li, layer in enumerate(seq.layers):
+                view = layer.append_for_attention(kn[li], vn[li])
+                outs[li] = compressed_kv_decode(q[li], view, SCALE)
+                layer.compact_residual()
+        host_out.copy_(torch.stack(outs))   # blocking read of the step's result
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+    seq.rollback()
+    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
+    d2h = host_out.numel() * 2
+
+    # ---- roofline of the decode kernel -----------------------------------------
+    sec, bytes_per_launch = time_kernel(seq, decode)
+    peak, peak_kind = peaks()
+    achieved = bytes_per_launch / sec / 1e9
+    traffic = None
+    tfile = ROOT / 'profiles' / 'traffic_attn_q8_decode.json'
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get('bytes_per_launch')
+
+    us_step = ms * 1e3 / args.steps
+    value = world * args.steps / (ms * 1e-3)
+    line = {'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms / args.steps,
+            'us_per_step': us_step, 'us_per_layer': us_step / LAYERS,
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'u8/bf16', 'data': 'synthetic (seeded N(0,1), 1% outlier channels x8)',
+            'config': config(args, world),
+            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
+                         'frac': achieved / peak, 'traffic': traffic, 'peak_source': peak_kind,
+                         'kernel': 'attn_kernel<8,256,1,bf16>',
+                         'bytes_per_launch': bytes_per_launch, 'us_per_launch': sec * 1e6},
+            'hbm_gbs_step': world * LAYERS * bytes_per_launch * args.steps / (ms * 1e-3) / 1e9 / world,
+            'clocks': clk,
+            'e2e': {'value': world * e2e_steps / (e2e_ms * 1e-3), 'unit': 'tok/s',
+                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                    'us_per_step': e2e_ms * 1e3 / e2e_steps},
+            'gpu_launches': launches}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        del seq
+        torch.cuda.empty_cache()
+        base = cpu_reference(args.cpu_steps, 1)
+        line['cpu_baseline'] = {k: base[k] for k in ('value', 'unit', 'cores', 'kind', 'sample')}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=1024)
+    ap.add_argument('--warmup', type=int, default=16)
+    ap.add_argument('--impl', choices=('b200', 'reference'), default='b200')
+    ap.add_argument('--cpu-steps', type=int, default=24)
+    ap.add_argument('--no-cpu', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error('--warmup must be >= 3')
+    world, rank, local = init_dist()
+    try:
+        if args.impl == 'reference':
+            reference_arm(args, world, rank)
+        else:
+            b200_arm(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    sys.path.insert(0, str(ROOT))
+    main()

@@ -1,0 +1,189 @@
+/*
+ * ckv.h -- C ABI of the B200 compressed-KV library (libtrpg_ckv.so).
+ *
+ * Plain pointers, sizes and strides only; every entry point returns a
+ * ckv_status and never allocates device memory.  All device pointers must be
+ * resident on the current CUDA device; work is enqueued on `stream` and the
+ * functions return without synchronising.
+ *
+ * Cache layout (unchanged from the reference, models/quantized_kv.py:43-66):
+ *   key codes   uint8 [B,H,Ucap,D,128/(8/bits)]  one row = one channel over
+ *               a 128-token block; Q4 keeps token 2j in the low nibble of
+ *               byte j, token 2j+1 in the high nibble
+ *   key meta    fp32  [B,H,Ucap,D,2]              (scale, low) per row
+ *   value codes uint8 [B,H,Tcap,D/64,64/(8/bits)] one row = one token over a
+ *               64-channel group; Q4 keeps channel 2j low, 2j+1 high
+ *   value meta  fp32  [B,H,Tcap,D/64,2]
+ *   residual    bf16|fp16 [B,H,R,D]               exact recent window
+ * Inner dimensions (the last two of every bank) must be dense; head and
+ * unit/token strides are free (slab capacity).  All strides are in elements
+ * of their own tensor.
+ */
+#ifndef TRPG_CKV_H
+#define TRPG_CKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ckv_stream_t; /* identical to cudaStream_t */
+
+typedef enum {
+  CKV_OK = 0,
+  CKV_ERR_INVALID = 1,     /* bad pointer, size, stride or alignment */
+  CKV_ERR_UNSUPPORTED = 2, /* valid request this build has no kernel for */
+  CKV_ERR_WORKSPACE = 3,   /* workspace missing or too small */
+  CKV_ERR_CUDA = 4         /* a CUDA call or launch failed */
+} ckv_status;
+
+typedef enum { CKV_BF16 = 0, CKV_F16 = 1 } ckv_dtype;
+typedef enum { CKV_ROUND_HALF_EVEN = 0, CKV_ROUND_HALF_UP = 1 } ckv_rounding;
+
+/* Human-readable text for a status code (static storage). */
+const char *ckv_status_string(int status);
+/* Last CUDA error string recorded by this thread, or "" (static storage). */
+const char *ckv_last_error(void);
+/* ABI version: (major << 16) | minor. */
+int ckv_version(void);
+
+/* ---------------------------------------------------------------------- */
+/* Quantizer                                                               */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Affine-quantize `rows` dense rows of `group` (64 or 128) elements each.
+ * Per row: low = min, scale = max((max - low) / (2^bits - 1), 1e-8),
+ * code = clamp(round((x - low) / scale), 0, 2^bits - 1) with IEEE fp32
+ * arithmetic; `rounding` selects half-to-even (the reference CPU quantizer,
+ * models/quantized_kv.py:19-25) or half-up (the reference Triton kernel,
+ * models/quantized_kv_kernels.py:7-22).  Q4 packs code 2j | code 2j+1 << 4.
+ * Replaces models/quantized_kv_kernels.py:39 `pack(rows, bits)`.
+ * codes: rows*group*bits/8 bytes; meta: rows*2 floats (scale, low).
+ */
+int ckv_pack_rows(const void *x, int dtype, int64_t rows, int group, int bits,
+                  int rounding, uint8_t *codes, float *meta, ckv_stream_t stream);
+
+/*
+ * Dequantize: out = round_to_dtype(fma(code, scale, low)), one rounding of
+ * the fused multiply-add, as the reference CUDA path does.
+ * Replaces models/quantized_kv_kernels.py:50 `unpack(data, meta, bits, dtype)`.
+ */
+int ckv_unpack_rows(const uint8_t *codes, const float *meta, int64_t rows, int group,
+                    int bits, int dtype, void *out, ckv_stream_t stream);
+
+/* Direct-to-slab bank append: quantize `count` (a multiple of 128) tokens of
+ * one sequence's residual window straight into the key and value banks at
+ * unit `unit_offset` (token unit_offset*128).  Same arithmetic as
+ * ckv_pack_rows; replaces the pack + copy_ pair of
+ * models/quantized_kv.py:43-66 (`_PackedBank.append`). */
+typedef struct {
+  const void *keys;    /* residual [H,R,D]: strides below, last dim dense */
+  const void *values;
+  int64_t k_stride_head, k_stride_token;
+  int64_t v_stride_head, v_stride_token;
+  uint8_t *key_data;   /* bank base pointers (batch index 0) */
+  float *key_meta;
+  uint8_t *value_data;
+  float *value_meta;
+  int64_t kd_stride_head, kd_stride_unit;   /* key codes: dims 1 and 2 */
+  int64_t km_stride_head, km_stride_unit;
+  int64_t vd_stride_head, vd_stride_token;
+  int64_t vm_stride_head, vm_stride_token;
+  int32_t heads, head_dim, bits, dtype, rounding;
+  int32_t count;        /* tokens to quantize, multiple of 128 */
+  int32_t unit_offset;  /* first destination unit */
+} ckv_append_args;
+
+int ckv_pack_append(const ckv_append_args *args, ckv_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Attention over a compressed view                                         */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * One sequence.  Queries attend to packed tokens [unit_begin*128,
+ * unit_end*128) and residual tokens [resid_begin, resid_end) (indices into
+ * the residual window; absolute position packed_tokens + index).  A full view
+ * uses unit_begin = 0, unit_end = packed_tokens/128, resid_begin = 0,
+ * resid_end = R.  A split-KV shard narrows the ranges.
+ * Query row (n, g) of KV head h is query head h*G + g, query position n
+ * (0..nq-1, the last nq positions of the sequence).  With nq > 1 the mask is
+ * lower-right causal: query n sees absolute position p iff
+ * p <= length - nq + n (models/compressed_prefill_kernels.py:81,90).
+ */
+typedef struct {
+  const void *query;            /* [Hq,nq,D] dtype, last dim dense */
+  int64_t q_stride_head, q_stride_pos;
+  const uint8_t *key_data;  int64_t kd_stride_head, kd_stride_unit;
+  const float *key_meta;    int64_t km_stride_head, km_stride_unit;
+  const uint8_t *value_data; int64_t vd_stride_head, vd_stride_token;
+  const float *value_meta;  int64_t vm_stride_head, vm_stride_token;
+  const void *keys;         int64_t rk_stride_head, rk_stride_token;
+  const void *values;       int64_t rv_stride_head, rv_stride_token;
+  int64_t packed_tokens;        /* P, a multiple of 128 */
+  int64_t length;               /* L = P + R */
+  int32_t unit_begin, unit_end;
+  int32_t resid_begin, resid_end;
+  void *out;                    /* normalized: [Hq,nq,D] dtype, dense
+                                   partial:    see ckv_attn_args.partial */
+} ckv_seq;
+
+typedef struct {
+  const ckv_seq *seqs;          /* host array of `num_seqs` descriptors */
+  int32_t num_seqs;
+  int32_t heads_q, heads_kv, head_dim, nq, bits, dtype;
+  float scale;                  /* softmax scale applied to q.k */
+  /* partial = 0: write normalized outputs to seqs[i].out.
+   * partial = 1: write unnormalized split-KV partials, fp32, to
+   *   seqs[i].out laid out as [Hq*nq rows] x (D + 2): row (h*G+g)*nq... see
+   *   ckv_partial_row(); o[0..D) = sum 2^(s - m) v, then m (log2 domain,
+   *   -inf if the shard saw no token) and l = sum 2^(s - m). */
+  int32_t partial;
+  int32_t flags;                /* CKV_WS_COUNTERS_ZERO, ... */
+} ckv_attn_args;
+
+#define CKV_WS_COUNTERS_ZERO 1  /* caller guarantees the workspace counter
+                                   region is zero; the call leaves it zero */
+
+/* Maximum sequences in one ckv_attention call. */
+#define CKV_MAX_SEQS 96
+
+/* Bytes of workspace ckv_attention needs for `args` (host-only, no CUDA). */
+int ckv_attention_workspace(const ckv_attn_args *args, size_t *bytes);
+
+/*
+ * Split-KV GQA attention over compressed views (decode when nq == 1,
+ * multi-query verify when nq > 1).  Dequantizes in registers with the
+ * reference's rounding (fma then round to the query dtype,
+ * models/compressed_kv_kernels.py:47,68), online softmax in the log2 domain
+ * (:51-58), fp32 accumulation, and merges split partials with the
+ * log-sum-exp rule of :85-89 inside the same launch.  Replaces
+ * models/compressed_kv_kernels.py:93 `decode(query, view, scale)` and, for
+ * nq > 1, the dequantize + SDPA(causal_lower_right) verify path
+ * (models/quantized_kv.py:126-134 then scaled_dot_product_attention).
+ * workspace: ckv_attention_workspace() bytes, 256-byte aligned.
+ */
+int ckv_attention(const ckv_attn_args *args, void *workspace, size_t workspace_bytes,
+                  ckv_stream_t stream);
+
+/* Row index of (query head hq, position n) in a partial buffer. */
+static inline int64_t ckv_partial_row(int hq, int n, int nq) { return (int64_t)hq * nq + n; }
+
+/*
+ * Merge `parts` split-KV partials (each rows x (D+2) fp32 as written by
+ * ckv_attention with partial = 1, stored back to back in `partials`) into
+ * normalized outputs [rows, D] of `dtype`.  Same rule as
+ * models/compressed_kv_kernels.py:85-89; shards that saw no token (m = -inf)
+ * get weight 0.
+ */
+int ckv_combine_partials(const float *partials, int parts, int64_t rows, int head_dim,
+                         int dtype, void *out, ckv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRPG_CKV_H */

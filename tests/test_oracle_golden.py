@@ -76,3 +76,23 @@ def test_cache_state_and_attention_match_reference(name):
     got = O.decode_reference(q, layer, scale, fused=False)
     want = A[f'{name}_output']
     np.testing.assert_allclose(got, want, rtol=1e-2, atol=4e-3)
+
+
+@pytest.mark.parametrize('name', ['c1_q8_l2048', 'q4_l2048', 'verify_q8_n4_l1500'])
+def test_cpu_timing_path_matches_reference(name):
+    """The torch-CPU restatement used for CPU timings reproduces the reference."""
+    import torch
+    from oracle import ckv_cpu_path as P
+    bits, hkv, hq, length, dim, n, seed, outliers = (int(x) for x in A[f'{name}_spec'])
+    dtype = str(A[f'{name}_dtype'])
+    tdt = getattr(torch, dtype)
+    _, k, v = O.cache_state(seed, hkv, length, dim, bits, n, dtype, outliers=bool(outliers))
+    layer = P.CpuLayer(bits)
+    kt, vt = torch.from_numpy(k).to(tdt), torch.from_numpy(v).to(tdt)
+    layer.update(kt[:, :, :length - n], vt[:, :, :length - n])
+    layer.append_for_attention(kt[:, :, length - n:], vt[:, :, length - n:])
+    assert O.digest(layer.kd.numpy(), layer.km.numpy(), layer.vd.numpy(),
+                    layer.vm.numpy()) == str(A[f'{name}_bank_digest'])
+    q = torch.from_numpy(O.seeded_normal(seed + 2, (1, hq, n, dim), dtype)).to(tdt)
+    out = P.attend(q, layer, float(A[f'{name}_scale'])).float().numpy()
+    np.testing.assert_array_equal(out, A[f'{name}_output'])

@@ -1,0 +1,56 @@
+"""Loader for the in-tree native libraries.
+
+``libtrpg_ckv.so`` holds the CUDA kernels behind the C ABI of
+``include/ckv.h``; ``_ckv_torch.so`` registers them as ``torch.ops.ckv.*``.
+There is no CPU implementation and no fallback: if either library is
+missing, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / 'libtrpg_ckv.so'
+TORCH_LIB_PATH = PKG / '_ckv_torch.so'
+
+# Symbols of include/ckv.h, in declaration order.
+EXPORTS = ('ckv_status_string', 'ckv_last_error', 'ckv_version', 'ckv_pack_rows',
+           'ckv_unpack_rows', 'ckv_pack_append', 'ckv_attention_workspace', 'ckv_attention',
+           'ckv_combine_partials')
+
+ROUNDING = {'half_even': 0, 'half_up': 1}
+
+_lib = None
+_loaded = False
+
+
+def library() -> ctypes.CDLL:
+    """The C-ABI library (ctypes handle)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f'{LIB_PATH.name} is not built; run `python -m trpg_b200.build`')
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        _lib.ckv_status_string.restype = ctypes.c_char_p
+        _lib.ckv_last_error.restype = ctypes.c_char_p
+    return _lib
+
+
+def load() -> None:
+    """Register ``torch.ops.ckv``; raises ImportError when not built."""
+    global _loaded
+    if _loaded:
+        return
+    library()
+    if not TORCH_LIB_PATH.exists():
+        raise ImportError(f'{TORCH_LIB_PATH.name} is not built; run `python -m trpg_b200.build`')
+    torch.ops.load_library(str(TORCH_LIB_PATH))
+    _loaded = True
+
+
+def ops():
+    load()
+    return torch.ops.ckv

@@ -1,0 +1,173 @@
+"""Guarded compressed-KV attention entry points and the attention-module patch.
+
+Mirror of ``models/compressed_kv_attention.py`` over the B200 kernels:
+
+* ``compressed_kv_decode(query, view, scale)`` -- the same eligibility guard
+  as the reference (``:8-29``); returns ``None`` for anything the kernel does
+  not cover so the caller falls back to SDPA.
+* ``compressed_kv_verify(query, view, scale)`` -- new: the multi-query
+  (MTP verify) variant, 2..16 query rows per KV head, lower-right causal.
+* ``_supported_mask`` (``:32-37``), ``_forward`` (``:40-82``),
+  ``configure_compressed_kv_attention`` (``:85-95``) and
+  ``compressed_kv_info`` (``:98-103``).  ``_forward`` additionally routes
+  2..4-token calls to ``compressed_kv_verify`` inside
+  ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``).
+
+Kernel launch errors raise; only "unsupported" returns ``None``.
+"""
+from __future__ import annotations
+
+import math
+from types import MethodType
+
+import torch
+
+from .mtp_verification_kernels import mtp_verification_enabled
+from .quantized_kv import QuantizedAttentionLayer
+
+BACKEND = 'b200-affine-q4-q8-cuda'
+
+
+def _view_ok(query, view, min_residual):
+    if view.bits not in (4, 8) or not math.isfinite(view.length):
+        return False
+    tensors = (view.keys, view.values, view.key_data, view.key_meta, view.value_data, view.value_meta)
+    if any(t is None or t.device != query.device or t.requires_grad for t in tensors):
+        return False
+    if (view.keys.ndim != 4 or view.values.shape != view.keys.shape or view.keys.shape[0] != 1
+            or view.keys.dtype != query.dtype or view.values.dtype != query.dtype
+            or view.keys.shape[-1] != query.shape[-1] or query.shape[1] % view.keys.shape[1]
+            or view.length != view.packed_tokens + view.keys.shape[2]
+            or view.keys.shape[2] < min_residual
+            or view.keys.stride(-1) != 1 or view.values.stride(-1) != 1):
+        return False
+    return True
+
+
+def _query_ok(query, scale):
+    return (query.is_cuda and not torch.is_grad_enabled() and not torch.is_autocast_enabled('cuda')
+            and query.ndim == 4 and query.shape[0] == 1
+            and query.dtype in (torch.bfloat16, torch.float16) and query.stride(-1) == 1
+            and query.shape[-1] in (64, 128, 256) and not query.requires_grad
+            and math.isfinite(scale))
+
+
+def compressed_kv_decode(query, view, scale):
+    """Single-query decode, or None when unsupported (reference ``:8-29``)."""
+    if not _query_ok(query, scale) or query.shape[2] != 1 or view.packed_tokens < 128:
+        return None
+    if not _view_ok(query, view, 0) or query.shape[1] // view.keys.shape[1] > 16:
+        return None
+    try:
+        from .compressed_kv_kernels import decode
+    except ImportError:
+        return None
+    return decode(query, view, scale)
+
+
+def compressed_kv_verify(query, view, scale):
+    """Multi-query verify over a packed view, or None when unsupported.
+
+    query [1, Hq, n, D] holds the last n positions (already appended to the
+    view's residual); rows n * Hq/Hkv must not exceed 16.
+    """
+    if not _query_ok(query, scale) or query.shape[2] < 1 or view.packed_tokens < 128:
+        return None
+    if not _view_ok(query, view, query.shape[2]):
+        return None
+    if query.shape[2] * (query.shape[1] // view.keys.shape[1]) > 16:
+        return None
+    try:
+        from .compressed_kv_kernels import verify
+    except ImportError:
+        return None
+    return verify(query, view, scale)
+
+
+def _supported_mask(mask, length, queries=1):
+    """None, or a lower-right causal bias of ``queries`` x ``length`` (``:32-37``)."""
+    if mask is None:
+        return True
+    from torch.nn.attention.bias import CausalBias, CausalVariant
+    return (type(mask) is CausalBias and mask.variant == CausalVariant.LOWER_RIGHT
+            and mask.seq_len_q == queries and mask.seq_len_kv == length)
+
+
+def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_values=None, **kwargs):
+    """Patched ``Qwen3_5Attention.forward`` (reference ``:40-82``)."""
+    layer = None
+    if past_key_values is not None and self.layer_idx < len(past_key_values.layers):
+        layer = past_key_values.layers[self.layer_idx]
+    q_len = hidden_states.shape[1] if hidden_states.ndim == 3 else 0
+    verify = q_len > 1 and q_len <= 4 and mtp_verification_enabled()
+    eligible = (self._direct_kv_enabled and not self.training and not torch.is_grad_enabled()
+                and not torch.is_autocast_enabled('cuda') and hidden_states.is_cuda
+                and hidden_states.shape[0] == 1 and (q_len == 1 or verify)
+                and hidden_states.dtype in (torch.bfloat16, torch.float16)
+                and isinstance(layer, QuantizedAttentionLayer) and layer.key_bank.units > 0
+                and self.head_dim in (64, 128, 256) and self.config._attn_implementation == 'sdpa'
+                and not kwargs.get('output_attentions', False) and kwargs.get('head_mask') is None
+                and all(value is None or name in ('is_causal', 'output_attentions', 'use_cache', 'position_ids')
+                        for name, value in kwargs.items())
+                and _supported_mask(attention_mask, layer.get_seq_length() + q_len, q_len))
+    if not eligible:
+        return self._direct_kv_original(hidden_states, position_embeddings, attention_mask,
+                                        past_key_values=past_key_values, **kwargs)
+    from transformers.models.qwen3_5.modeling_qwen3_5 import apply_rotary_pos_emb
+    shape = hidden_states.shape[:-1]
+    head_shape = (*shape, -1, self.head_dim)
+    query, gate = torch.chunk(self.q_proj(hidden_states).view(*shape, -1, self.head_dim * 2), 2, -1)
+    gate = gate.reshape(*shape, -1)
+    query = self.q_norm(query.reshape(head_shape)).transpose(1, 2)
+    key = self.k_norm(self.k_proj(hidden_states).view(head_shape)).transpose(1, 2)
+    value = self.v_proj(hidden_states).view(head_shape).transpose(1, 2)
+    query, key = apply_rotary_pos_emb(query, key, *position_embeddings)
+    view = layer.append_for_attention(key, value)
+    if q_len == 1:
+        output = compressed_kv_decode(query, view, self.scaling)
+    else:
+        output = compressed_kv_verify(query, view, self.scaling)
+    if output is None:
+        # State was appended once: finish the same operation with SDPA rather
+        # than running upstream and appending these tokens a second time.
+        keys = torch.cat((layer.key_bank.unpack(layer.dtype), view.keys), -2)
+        values = torch.cat((layer.value_bank.unpack(layer.dtype), view.values), -2)
+        mask = None
+        if q_len > 1:
+            from torch.nn.attention.bias import causal_lower_right
+            mask = causal_lower_right(q_len, view.length)
+        output = torch.nn.functional.scaled_dot_product_attention(query, keys, values, attn_mask=mask,
+                                                                  enable_gqa=True, scale=self.scaling)
+    else:
+        self._direct_kv_calls += 1
+        if q_len > 1:
+            self._direct_kv_verify_calls += 1
+        self._direct_kv_last_length = view.length
+    layer.compact_residual()
+    output = output.transpose(1, 2).reshape(*shape, -1).contiguous()
+    return self.o_proj(output * torch.sigmoid(gate)), None
+
+
+def configure_compressed_kv_attention(model, enabled=True):
+    """Patch every ``Qwen3_5Attention`` (reference ``:85-95``)."""
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
+    for module in model.modules():
+        if type(module) is not Qwen3_5Attention:
+            continue
+        if not hasattr(module, '_direct_kv_original'):
+            module._direct_kv_original = module.forward
+            module._direct_kv_calls = module._direct_kv_last_length = 0
+            module._direct_kv_verify_calls = 0
+            module.forward = MethodType(_forward, module)
+        module._direct_kv_enabled = bool(enabled)
+    return compressed_kv_info(model)
+
+
+def compressed_kv_info(model):
+    """Dispatch counters (reference ``:98-103``)."""
+    modules = [m for m in model.modules() if hasattr(m, '_direct_kv_enabled')]
+    return dict(backend=BACKEND, configured_layers=sum(m._direct_kv_enabled for m in modules),
+                direct_decode_calls=sum(m._direct_kv_calls for m in modules),
+                direct_verify_calls=sum(getattr(m, '_direct_kv_verify_calls', 0) for m in modules),
+                longest_decode=max((m._direct_kv_last_length for m in modules), default=0),
+                fallback='SDPA for prefill, arbitrary masks, unsupported shapes or precision')

@@ -1,0 +1,102 @@
+"""Drop-in for ``models/compressed_kv_kernels.py``: attention over packed views.
+
+``decode(query, view, scale)`` keeps the reference signature and return
+convention (``models/compressed_kv_kernels.py:93``): a new tensor shaped and
+typed like ``query``; the view is not modified.  It runs one launch of the
+hand-written sm_100a kernel behind ``ckv_attention`` (``include/ckv.h``):
+split-KV over (KV head, 128-token block) work items, in-register dequant of
+the Q8/Q4 history next to the exact residual window, and the log-sum-exp
+merge of the splits inside the same launch.
+
+Beyond the reference:
+
+* ``verify(query, view, scale)`` -- 2..4 (up to 16 rows per KV head) queries
+  with lower-right causal masking, the semantics of dequantize + SDPA with
+  ``causal_lower_right(q, L)`` (``models/quantized_kv.py:126-134``;
+  ``models/compressed_prefill_kernels.py:81,90``);
+* ``attention(queries, views, scale)`` -- many sequences (ragged lengths) in
+  one launch;
+* ``partial=True`` / ``ranges`` -- split-KV partials (m, l, o) of a shard of
+  the packed blocks and residual, merged by ``combine``.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from ._native import ops
+
+
+def _inner_dense(t: torch.Tensor) -> torch.Tensor:
+    """Banks need dense inner two dims and 16-byte aligned rows."""
+    if t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]:
+        t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone(memory_format=torch.contiguous_format)
+    return t
+
+
+def _residual(t: torch.Tensor) -> torch.Tensor:
+    if t.stride(-1) != 1 or t.stride(-2) % 8 or t.stride(-3) % 8 or t.data_ptr() % 16:
+        t = t.contiguous()
+        if t.data_ptr() % 16:
+            t = t.clone()
+    return t
+
+
+def full_range(view) -> list[int]:
+    """(unit_begin, unit_end, resid_begin, resid_end) covering the whole view."""
+    return [0, view.packed_tokens // 128, 0, view.keys.shape[2]]
+
+
+def attention(queries: Sequence[torch.Tensor], views: Sequence, scale: float, *,
+              ranges: Sequence[Sequence[int]] | None = None, partial: bool = False):
+    """One launch over every (query, view) pair.
+
+    queries[i]: [1, Hq, nq, D] (bf16/fp16, last dim dense); views[i]: a
+    ``QuantizedKVView``.  Returns a list of outputs shaped like the queries,
+    or, with ``partial=True``, float32 [Hq*nq, D+2] partials (o, m, l).
+    """
+    if len(queries) != len(views) or not queries:
+        raise ValueError('need one view per query')
+    bits = views[0].bits
+    kd, km, vd, vm, rk, rv, packed, lengths, flat = [], [], [], [], [], [], [], [], []
+    for i, (q, v) in enumerate(zip(queries, views)):
+        if v.bits != bits:
+            raise ValueError('all views of one call must share bits')
+        rng = list(ranges[i]) if ranges is not None else full_range(v)
+        has_packed = rng[1] > rng[0]
+        kd.append(_inner_dense(v.key_data) if has_packed else None)
+        km.append(_inner_dense(v.key_meta) if has_packed else None)
+        vd.append(_inner_dense(v.value_data) if has_packed else None)
+        vm.append(_inner_dense(v.value_meta) if has_packed else None)
+        has_resid = rng[3] > rng[2]
+        rk.append(_residual(v.keys) if has_resid else None)
+        rv.append(_residual(v.values) if has_resid else None)
+        packed.append(int(v.packed_tokens))
+        lengths.append(int(v.length))
+        flat.extend(int(x) for x in rng)
+    return ops().attention(list(queries), kd, km, vd, vm, rk, rv, packed, lengths, flat, int(bits),
+                           float(scale), bool(partial))
+
+
+def decode(query: torch.Tensor, view, scale: float) -> torch.Tensor:
+    """Single-query GQA decode over a packed view (``compressed_kv_kernels.py:93``)."""
+    return attention([query], [view], scale)[0]
+
+
+def verify(query: torch.Tensor, view, scale: float) -> torch.Tensor:
+    """Multi-query verify: lower-right causal attention of query [1,Hq,n,D]."""
+    return attention([query], [view], scale)[0]
+
+
+def combine(partials: Sequence[torch.Tensor] | torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Log-sum-exp merge of split-KV partials (``compressed_kv_kernels.py:85-89``).
+
+    partials: list of [rows, D+2] float32 (or one [parts, rows, D+2] tensor).
+    Returns [rows, D] of ``dtype``.
+    """
+    if not isinstance(partials, torch.Tensor):
+        partials = torch.stack(list(partials))
+    return ops().combine_partials(partials, dtype)

@@ -1,0 +1,301 @@
+// Quantize-on-append and dequantize kernels for the compressed KV cache.
+//
+// Arithmetic follows models/quantized_kv.py:19-25 (CPU quantizer: IEEE
+// division, round half to even) and models/quantized_kv_kernels.py:11-21
+// (Triton kernel: the same with floor(t + 0.5)); both are selectable.  All
+// divisions are correctly rounded (__fdiv_rn) and no multiply-add is
+// contracted, so results are bit-identical to the CPU reference.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ckv_common.cuh"
+
+namespace ckv {
+namespace {
+
+template <int BITS>
+__device__ __forceinline__ uint32_t quantize(float x, float low, float scale, int rounding) {
+  constexpr float kMax = float((1 << BITS) - 1);
+  float t = __fdiv_rn(__fsub_rn(x, low), scale);
+  float r = rounding == CKV_ROUND_HALF_EVEN ? rintf(t) : floorf(__fadd_rn(t, 0.5f));
+  r = fminf(fmaxf(r, 0.0f), kMax);
+  return static_cast<uint32_t>(r);
+}
+
+template <int BITS>
+__device__ __forceinline__ float group_scale(float mn, float mx) {
+  return fmaxf(__fdiv_rn(__fsub_rn(mx, mn), float((1 << BITS) - 1)), 1e-8f);
+}
+
+// One thread per row of G contiguous 16-bit values.
+template <int DT, int BITS, int G>
+__global__ void __launch_bounds__(128) pack_rows_kernel(const typename Elem<DT>::T *__restrict__ x,
+                                                        int64_t rows, int rounding,
+                                                        uint8_t *__restrict__ codes,
+                                                        float *__restrict__ meta) {
+  using E = Elem<DT>;
+  int64_t row = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + row * G);
+  float v[G];
+#pragma unroll
+  for (int i = 0; i < G / 8; ++i) {
+    uint4 w = src[i];
+    const typename E::T *h = reinterpret_cast<const typename E::T *>(&w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i * 8 + j] = E::to_f32(h[j]);
+  }
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < G; ++i) {
+    mn = fminf(mn, v[i]);
+    mx = fmaxf(mx, v[i]);
+  }
+  float scale = group_scale<BITS>(mn, mx);
+  constexpr int OUTB = G * BITS / 8;
+  uint4 *dst = reinterpret_cast<uint4 *>(codes + row * OUTB);
+#pragma unroll
+  for (int i = 0; i < OUTB / 16; ++i) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        int byte = i * 16 + k * 4 + b;
+        uint32_t val;
+        if constexpr (BITS == 8) {
+          val = quantize<8>(v[byte], mn, scale, rounding);
+        } else {
+          val = quantize<4>(v[2 * byte], mn, scale, rounding) |
+                (quantize<4>(v[2 * byte + 1], mn, scale, rounding) << 4);
+        }
+        word |= val << (8 * b);
+      }
+      w[k] = word;
+    }
+    dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  reinterpret_cast<float2 *>(meta)[row] = make_float2(scale, mn);
+}
+
+template <int DT, int BITS, int G>
+__global__ void __launch_bounds__(256) unpack_rows_kernel(const uint8_t *__restrict__ codes,
+                                                          const float *__restrict__ meta,
+                                                          int64_t total,
+                                                          typename Elem<DT>::T *__restrict__ out) {
+  using E = Elem<DT>;
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  int64_t row = i / G;
+  int col = int(i - row * G);
+  uint32_t code;
+  if constexpr (BITS == 8) {
+    code = codes[i];
+  } else {
+    code = (codes[row * (G / 2) + col / 2] >> ((col & 1) * 4)) & 15u;
+  }
+  float2 m = reinterpret_cast<const float2 *>(meta)[row];
+  out[i] = E::from_f32(__fmaf_rn(float(code), m.x, m.y));
+}
+
+// Direct-to-slab append.  Grid: (blocks of 128 tokens, heads).  Block 256
+// threads.  Key part: thread c < D quantizes channel c over the block's 128
+// tokens.  Value part: thread t quantizes token t's groups.
+template <int DT, int BITS, int D>
+__global__ void __launch_bounds__(256) append_kernel(ckv_append_args a) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  const int blk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int64_t tok0 = int64_t(blk) * 128;
+  const int unit = a.unit_offset + blk;
+  const T *keys = static_cast<const T *>(a.keys) + h * a.k_stride_head + tok0 * a.k_stride_token;
+  const T *values =
+      static_cast<const T *>(a.values) + h * a.v_stride_head + tok0 * a.v_stride_token;
+  constexpr int KS = 128 * BITS / 8;  // key bytes per channel row
+  if (tid < D) {
+    const int c = tid;
+    float mn = INFINITY, mx = -INFINITY;
+    for (int t = 0; t < 128; ++t) {
+      float v = E::to_f32(keys[t * a.k_stride_token + c]);
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+    float scale = group_scale<BITS>(mn, mx);
+    uint8_t *row = a.key_data + h * a.kd_stride_head + int64_t(unit) * a.kd_stride_unit + c * KS;
+    for (int i = 0; i < KS / 16; ++i) {
+      uint32_t w[4];
+      for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+        for (int b = 0; b < 4; ++b) {
+          int byte = i * 16 + k * 4 + b;
+          uint32_t val;
+          if constexpr (BITS == 8) {
+            val = quantize<8>(E::to_f32(keys[byte * a.k_stride_token + c]), mn, scale, a.rounding);
+          } else {
+            float x0 = E::to_f32(keys[(2 * byte) * a.k_stride_token + c]);
+            float x1 = E::to_f32(keys[(2 * byte + 1) * a.k_stride_token + c]);
+            val = quantize<4>(x0, mn, scale, a.rounding) |
+                  (quantize<4>(x1, mn, scale, a.rounding) << 4);
+          }
+          word |= val << (8 * b);
+        }
+        w[k] = word;
+      }
+      reinterpret_cast<uint4 *>(row)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    float *m = a.key_meta + h * a.km_stride_head + int64_t(unit) * a.km_stride_unit + c * 2;
+    reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+  }
+  // Values: 128 tokens x D/64 groups per block; each thread handles whole
+  // groups of 64 contiguous channels.
+  constexpr int NG = D / 64;
+  constexpr int VB = 64 * BITS / 8;  // value bytes per group
+  for (int task = tid; task < 128 * NG; task += blockDim.x) {
+    const int t = task / NG, g = task % NG;
+    const uint4 *src = reinterpret_cast<const uint4 *>(values + t * a.v_stride_token + g * 64);
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint4 w = src[i];
+      const T *hv = reinterpret_cast<const T *>(&w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i * 8 + j] = E::to_f32(hv[j]);
+    }
+    float mn = v[0], mx = v[0];
+#pragma unroll
+    for (int i = 1; i < 64; ++i) {
+      mn = fminf(mn, v[i]);
+      mx = fmaxf(mx, v[i]);
+    }
+    float scale = group_scale<BITS>(mn, mx);
+    const int64_t token = tok0 + t + int64_t(a.unit_offset) * 128;
+    uint8_t *dst = a.value_data + h * a.vd_stride_head + token * a.vd_stride_token + g * VB;
+#pragma unroll
+    for (int i = 0; i < VB / 16; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          int byte = i * 16 + k * 4 + b;
+          uint32_t val;
+          if constexpr (BITS == 8) {
+            val = quantize<8>(v[byte], mn, scale, a.rounding);
+          } else {
+            val = quantize<4>(v[2 * byte], mn, scale, a.rounding) |
+                  (quantize<4>(v[2 * byte + 1], mn, scale, a.rounding) << 4);
+          }
+          word |= val << (8 * b);
+        }
+        w[k] = word;
+      }
+      reinterpret_cast<uint4 *>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    float *m = a.value_meta + h * a.vm_stride_head + token * a.vm_stride_token + g * 2;
+    reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+  }
+}
+
+bool aligned(const void *p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+template <int DT, int BITS>
+int launch_pack_rows(const void *x, int64_t rows, int group, int rounding, uint8_t *codes,
+                     float *meta, cudaStream_t s) {
+  using T = typename Elem<DT>::T;
+  unsigned grid = unsigned((rows + 127) / 128);
+  if (group == 128)
+    pack_rows_kernel<DT, BITS, 128><<<grid, 128, 0, s>>>(static_cast<const T *>(x), rows, rounding,
+                                                          codes, meta);
+  else
+    pack_rows_kernel<DT, BITS, 64><<<grid, 128, 0, s>>>(static_cast<const T *>(x), rows, rounding,
+                                                         codes, meta);
+  return cuda_status(cudaGetLastError());
+}
+
+template <int DT, int BITS>
+int launch_unpack_rows(const uint8_t *codes, const float *meta, int64_t rows, int group, void *out,
+                       cudaStream_t s) {
+  using T = typename Elem<DT>::T;
+  int64_t total = rows * group;
+  unsigned grid = unsigned((total + 255) / 256);
+  if (group == 128)
+    unpack_rows_kernel<DT, BITS, 128><<<grid, 256, 0, s>>>(codes, meta, total, static_cast<T *>(out));
+  else
+    unpack_rows_kernel<DT, BITS, 64><<<grid, 256, 0, s>>>(codes, meta, total, static_cast<T *>(out));
+  return cuda_status(cudaGetLastError());
+}
+
+template <int DT, int BITS>
+int launch_append(const ckv_append_args &a, cudaStream_t s) {
+  dim3 grid(a.count / 128, a.heads);
+  switch (a.head_dim) {
+    case 64: append_kernel<DT, BITS, 64><<<grid, 256, 0, s>>>(a); break;
+    case 128: append_kernel<DT, BITS, 128><<<grid, 256, 0, s>>>(a); break;
+    case 256: append_kernel<DT, BITS, 256><<<grid, 256, 0, s>>>(a); break;
+    default: return CKV_ERR_UNSUPPORTED;
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace ckv
+
+using namespace ckv;
+
+extern "C" int ckv_pack_rows(const void *x, int dtype, int64_t rows, int group, int bits,
+                             int rounding, uint8_t *codes, float *meta, ckv_stream_t stream) {
+  if (rows < 0 || (group != 64 && group != 128) || (bits != 4 && bits != 8) ||
+      (dtype != CKV_BF16 && dtype != CKV_F16) ||
+      (rounding != CKV_ROUND_HALF_EVEN && rounding != CKV_ROUND_HALF_UP))
+    return CKV_ERR_INVALID;
+  if (rows == 0) return CKV_OK;
+  if (!x || !codes || !meta || !aligned(x, 16) || !aligned(codes, 16) || !aligned(meta, 8))
+    return CKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CKV_BF16)
+    return bits == 8 ? launch_pack_rows<CKV_BF16, 8>(x, rows, group, rounding, codes, meta, s)
+                     : launch_pack_rows<CKV_BF16, 4>(x, rows, group, rounding, codes, meta, s);
+  return bits == 8 ? launch_pack_rows<CKV_F16, 8>(x, rows, group, rounding, codes, meta, s)
+                   : launch_pack_rows<CKV_F16, 4>(x, rows, group, rounding, codes, meta, s);
+}
+
+extern "C" int ckv_unpack_rows(const uint8_t *codes, const float *meta, int64_t rows, int group,
+                               int bits, int dtype, void *out, ckv_stream_t stream) {
+  if (rows < 0 || (group != 64 && group != 128) || (bits != 4 && bits != 8) ||
+      (dtype != CKV_BF16 && dtype != CKV_F16))
+    return CKV_ERR_INVALID;
+  if (rows == 0) return CKV_OK;
+  if (!codes || !meta || !out || !aligned(meta, 8)) return CKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == CKV_BF16)
+    return bits == 8 ? launch_unpack_rows<CKV_BF16, 8>(codes, meta, rows, group, out, s)
+                     : launch_unpack_rows<CKV_BF16, 4>(codes, meta, rows, group, out, s);
+  return bits == 8 ? launch_unpack_rows<CKV_F16, 8>(codes, meta, rows, group, out, s)
+                   : launch_unpack_rows<CKV_F16, 4>(codes, meta, rows, group, out, s);
+}
+
+extern "C" int ckv_pack_append(const ckv_append_args *args, ckv_stream_t stream) {
+  if (!args) return CKV_ERR_INVALID;
+  const ckv_append_args &a = *args;
+  if ((a.bits != 4 && a.bits != 8) || (a.dtype != CKV_BF16 && a.dtype != CKV_F16) ||
+      (a.rounding != CKV_ROUND_HALF_EVEN && a.rounding != CKV_ROUND_HALF_UP) || a.count < 0 ||
+      a.count % 128 || a.heads <= 0 || a.unit_offset < 0)
+    return CKV_ERR_INVALID;
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256) return CKV_ERR_UNSUPPORTED;
+  if (a.count == 0) return CKV_OK;
+  if (!a.keys || !a.values || !a.key_data || !a.key_meta || !a.value_data || !a.value_meta)
+    return CKV_ERR_INVALID;
+  // 16-byte vector loads of value rows and stores of code rows.
+  if (!aligned(a.values, 16) || (a.v_stride_token * 2) % 16 || (a.v_stride_head * 2) % 16 ||
+      !aligned(a.key_data, 16) || (a.kd_stride_unit % 16) || (a.kd_stride_head % 16) ||
+      !aligned(a.value_data, 16) || (a.vd_stride_token % 16) || (a.vd_stride_head % 16) ||
+      !aligned(a.key_meta, 8) || !aligned(a.value_meta, 8) || (a.km_stride_unit % 2) ||
+      (a.km_stride_head % 2) || (a.vm_stride_token % 2) || (a.vm_stride_head % 2))
+    return CKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (a.dtype == CKV_BF16)
+    return a.bits == 8 ? launch_append<CKV_BF16, 8>(a, s) : launch_append<CKV_BF16, 4>(a, s);
+  return a.bits == 8 ? launch_append<CKV_F16, 8>(a, s) : launch_append<CKV_F16, 4>(a, s);
+}

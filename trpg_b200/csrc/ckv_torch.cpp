@@ -1,0 +1,366 @@
+// torch.library registration of the compressed-KV ops (namespace `ckv`).
+//
+// A thin layer: it checks tensor shapes, dtypes and devices, reads strides,
+// picks the current CUDA stream and calls the C ABI of libtrpg_ckv.so.  No
+// computation happens here and there is no CPU implementation.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <utility>
+#include <vector>
+
+#include "ckv.h"
+
+namespace {
+
+using at::Tensor;
+
+void check_status(int st, const char *what) {
+  TORCH_CHECK(st == CKV_OK, "ckv::", what, " failed: ", ckv_status_string(st),
+              (st == CKV_ERR_CUDA ? std::string(" (") + ckv_last_error() + ")" : std::string()));
+}
+
+int dtype_code(at::ScalarType t) {
+  if (t == at::kBFloat16) return CKV_BF16;
+  if (t == at::kHalf) return CKV_F16;
+  TORCH_CHECK(false, "ckv: expected bfloat16 or float16, got ", t);
+  return -1;
+}
+
+ckv_stream_t current_stream(const Tensor &t) {
+  return reinterpret_cast<ckv_stream_t>(c10::cuda::getCurrentCUDAStream(t.get_device()).stream());
+}
+
+void require_cuda(const Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_cuda(), "ckv: ", name, " must be a CUDA tensor (this library has no CPU path)");
+}
+
+// ---------------------------------------------------------------------------
+// Quantizer
+// ---------------------------------------------------------------------------
+std::tuple<Tensor, Tensor> pack_rows(const Tensor &rows, int64_t bits, int64_t rounding) {
+  require_cuda(rows, "rows");
+  TORCH_CHECK(rows.dim() >= 1, "ckv::pack_rows: rows must have a group dimension");
+  const int64_t group = rows.size(-1);
+  TORCH_CHECK(group == 64 || group == 128, "ckv::pack_rows: group must be 64 or 128, got ", group);
+  TORCH_CHECK(bits == 4 || bits == 8, "ckv::pack_rows: bits must be 4 or 8");
+  c10::cuda::CUDAGuard guard(rows.device());
+  Tensor x = rows.contiguous();
+  auto shape = x.sizes().vec();
+  shape.back() = group * bits / 8;
+  Tensor codes = at::empty(shape, x.options().dtype(at::kByte));
+  shape.back() = 2;
+  Tensor meta = at::empty(shape, x.options().dtype(at::kFloat));
+  const int64_t n = x.numel() / group;
+  check_status(ckv_pack_rows(x.data_ptr(), dtype_code(x.scalar_type()), n, int(group), int(bits),
+                             int(rounding), codes.data_ptr<uint8_t>(), meta.data_ptr<float>(),
+                             current_stream(x)),
+               "pack_rows");
+  return {codes, meta};
+}
+
+Tensor unpack_rows(const Tensor &data, const Tensor &meta, int64_t bits, at::ScalarType dtype) {
+  require_cuda(data, "data");
+  require_cuda(meta, "meta");
+  TORCH_CHECK(data.scalar_type() == at::kByte && meta.scalar_type() == at::kFloat,
+              "ckv::unpack_rows: data must be uint8 and meta float32");
+  TORCH_CHECK(bits == 4 || bits == 8, "ckv::unpack_rows: bits must be 4 or 8");
+  c10::cuda::CUDAGuard guard(data.device());
+  Tensor d = data.contiguous(), m = meta.contiguous();
+  const int64_t group = d.size(-1) * (bits == 4 ? 2 : 1);
+  TORCH_CHECK(m.size(-1) == 2 && m.numel() * group / 2 == d.numel() * (bits == 4 ? 2 : 1),
+              "ckv::unpack_rows: meta must hold (scale, low) per row");
+  auto shape = d.sizes().vec();
+  shape.back() = group;
+  Tensor out = at::empty(shape, d.options().dtype(dtype));
+  check_status(ckv_unpack_rows(d.data_ptr<uint8_t>(), m.data_ptr<float>(), d.numel() * 8 / bits / group,
+                               int(group), int(bits), dtype_code(dtype), out.data_ptr(),
+                               current_stream(d)),
+               "unpack_rows");
+  return out;
+}
+
+// Quantize residual tokens [0, count) of keys/values [1,H,R,D] into the banks
+// at unit `unit_offset`.  Banks: key [1,H,U,D,S], value [1,H,T,D/64,S'].
+void pack_append(const Tensor &keys, const Tensor &values, const Tensor &kd, const Tensor &km,
+                 const Tensor &vd, const Tensor &vm, int64_t count, int64_t unit_offset,
+                 int64_t bits, int64_t rounding) {
+  for (auto *t : {&keys, &values, &kd, &km, &vd, &vm}) require_cuda(*t, "append tensor");
+  TORCH_CHECK(keys.dim() == 4 && values.sizes() == keys.sizes() && keys.size(0) == 1,
+              "ckv::pack_append: keys/values must be [1,H,R,D]");
+  TORCH_CHECK(keys.scalar_type() == values.scalar_type(), "ckv::pack_append: dtype mismatch");
+  TORCH_CHECK(keys.stride(-1) == 1 && values.stride(-1) == 1, "ckv::pack_append: last dim dense");
+  TORCH_CHECK(count >= 0 && count % 128 == 0 && count <= keys.size(2),
+              "ckv::pack_append: count must be a multiple of 128 within the residual");
+  const int64_t H = keys.size(1), D = keys.size(3), S = 128 * bits / 8, SV = 64 * bits / 8;
+  TORCH_CHECK(kd.dim() == 5 && kd.size(1) == H && kd.size(3) == D && kd.size(4) == S &&
+                  kd.stride(4) == 1 && kd.stride(3) == S && kd.scalar_type() == at::kByte,
+              "ckv::pack_append: key bank must be uint8 [1,H,U,D,", S, "] with dense inner dims");
+  TORCH_CHECK(km.dim() == 5 && km.size(1) == H && km.size(3) == D && km.size(4) == 2 &&
+                  km.stride(4) == 1 && km.stride(3) == 2 && km.scalar_type() == at::kFloat,
+              "ckv::pack_append: key meta must be float32 [1,H,U,D,2]");
+  TORCH_CHECK(vd.dim() == 5 && vd.size(1) == H && vd.size(3) == D / 64 && vd.size(4) == SV &&
+                  vd.stride(4) == 1 && vd.stride(3) == SV && vd.scalar_type() == at::kByte,
+              "ckv::pack_append: value bank must be uint8 [1,H,T,D/64,", SV, "]");
+  TORCH_CHECK(vm.dim() == 5 && vm.size(1) == H && vm.size(3) == D / 64 && vm.size(4) == 2 &&
+                  vm.stride(4) == 1 && vm.stride(3) == 2 && vm.scalar_type() == at::kFloat,
+              "ckv::pack_append: value meta must be float32 [1,H,T,D/64,2]");
+  TORCH_CHECK(unit_offset >= 0 && unit_offset + count / 128 <= kd.size(2) &&
+                  unit_offset + count / 128 <= km.size(2) &&
+                  (unit_offset * 128 + count) <= vd.size(2) && (unit_offset * 128 + count) <= vm.size(2),
+              "ckv::pack_append: bank capacity exceeded");
+  if (count == 0) return;
+  c10::cuda::CUDAGuard guard(keys.device());
+  ckv_append_args a{};
+  a.keys = keys.data_ptr();
+  a.values = values.data_ptr();
+  a.k_stride_head = keys.stride(1);
+  a.k_stride_token = keys.stride(2);
+  a.v_stride_head = values.stride(1);
+  a.v_stride_token = values.stride(2);
+  a.key_data = kd.data_ptr<uint8_t>();
+  a.key_meta = km.data_ptr<float>();
+  a.value_data = vd.data_ptr<uint8_t>();
+  a.value_meta = vm.data_ptr<float>();
+  a.kd_stride_head = kd.stride(1);
+  a.kd_stride_unit = kd.stride(2);
+  a.km_stride_head = km.stride(1);
+  a.km_stride_unit = km.stride(2);
+  a.vd_stride_head = vd.stride(1);
+  a.vd_stride_token = vd.stride(2);
+  a.vm_stride_head = vm.stride(1);
+  a.vm_stride_token = vm.stride(2);
+  a.heads = int(H);
+  a.head_dim = int(D);
+  a.bits = int(bits);
+  a.dtype = dtype_code(keys.scalar_type());
+  a.rounding = int(rounding);
+  a.count = int(count);
+  a.unit_offset = int(unit_offset);
+  check_status(ckv_pack_append(&a, current_stream(keys)), "pack_append");
+}
+
+// ---------------------------------------------------------------------------
+// Attention
+// ---------------------------------------------------------------------------
+
+// One persistent workspace per (device, stream): calls on one stream are
+// ordered, and every call leaves the counter region at zero.
+struct Workspace {
+  std::mutex mu;
+  std::map<std::pair<int, cudaStream_t>, Tensor> buffers;
+};
+Workspace &workspaces() {
+  static Workspace *w = new Workspace();
+  return *w;
+}
+
+Tensor workspace_for(const Tensor &like, size_t bytes) {
+  auto stream = c10::cuda::getCurrentCUDAStream(like.get_device());
+  auto key = std::make_pair(int(like.get_device()), stream.stream());
+  auto &ws = workspaces();
+  std::lock_guard<std::mutex> lock(ws.mu);
+  auto it = ws.buffers.find(key);
+  if (it != ws.buffers.end() && size_t(it->second.numel()) >= bytes) return it->second;
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(stream.stream(), &status);
+  TORCH_CHECK(status == cudaStreamCaptureStatusNone,
+              "ckv: the attention workspace must be allocated before stream capture; run one "
+              "call of the same (or larger) size on this stream first");
+  size_t cap = std::max<size_t>(bytes, size_t(1) << 20);
+  cap = (cap + (1 << 20) - 1) / (1 << 20) * (1 << 20);
+  Tensor t = at::zeros({int64_t(cap)}, like.options().dtype(at::kByte));
+  ws.buffers[key] = t;
+  return t;
+}
+
+ckv_seq make_seq(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor &vd,
+                 const Tensor &vm, const Tensor &rk, const Tensor &rv, int64_t packed,
+                 int64_t length, const int64_t *range, int64_t bits, int64_t hkv) {
+  const int64_t D = q.size(3), S = 128 * bits / 8, SV = 64 * bits / 8;
+  ckv_seq s{};
+  s.query = q.data_ptr();
+  s.q_stride_head = q.stride(1);
+  s.q_stride_pos = q.stride(2);
+  s.packed_tokens = packed;
+  s.length = length;
+  s.unit_begin = int32_t(range[0]);
+  s.unit_end = int32_t(range[1]);
+  s.resid_begin = int32_t(range[2]);
+  s.resid_end = int32_t(range[3]);
+  if (range[1] > range[0]) {
+    TORCH_CHECK(kd.defined() && km.defined() && vd.defined() && vm.defined(),
+                "ckv::attention: packed range needs the banks");
+    TORCH_CHECK(kd.scalar_type() == at::kByte && vd.scalar_type() == at::kByte &&
+                    km.scalar_type() == at::kFloat && vm.scalar_type() == at::kFloat,
+                "ckv::attention: banks must be uint8 codes with float32 meta");
+    TORCH_CHECK(kd.dim() == 5 && kd.size(1) == hkv && kd.size(3) == D && kd.size(4) == S &&
+                    kd.stride(4) == 1 && kd.stride(3) == S && kd.size(2) >= range[1],
+                "ckv::attention: key codes must be [1,H,U,D,", S, "] with dense inner dims");
+    TORCH_CHECK(km.dim() == 5 && km.size(1) == hkv && km.size(3) == D && km.size(4) == 2 &&
+                    km.stride(4) == 1 && km.stride(3) == 2 && km.size(2) >= range[1],
+                "ckv::attention: key meta must be [1,H,U,D,2] with dense inner dims");
+    TORCH_CHECK(vd.dim() == 5 && vd.size(1) == hkv && vd.size(3) == D / 64 && vd.size(4) == SV &&
+                    vd.stride(4) == 1 && vd.stride(3) == SV && vd.size(2) >= range[1] * 128,
+                "ckv::attention: value codes must be [1,H,T,D/64,", SV, "] with dense inner dims");
+    TORCH_CHECK(vm.dim() == 5 && vm.size(1) == hkv && vm.size(3) == D / 64 && vm.size(4) == 2 &&
+                    vm.stride(4) == 1 && vm.stride(3) == 2 && vm.size(2) >= range[1] * 128,
+                "ckv::attention: value meta must be [1,H,T,D/64,2] with dense inner dims");
+    s.key_data = kd.data_ptr<uint8_t>();
+    s.kd_stride_head = kd.stride(1);
+    s.kd_stride_unit = kd.stride(2);
+    s.key_meta = km.data_ptr<float>();
+    s.km_stride_head = km.stride(1);
+    s.km_stride_unit = km.stride(2);
+    s.value_data = vd.data_ptr<uint8_t>();
+    s.vd_stride_head = vd.stride(1);
+    s.vd_stride_token = vd.stride(2);
+    s.value_meta = vm.data_ptr<float>();
+    s.vm_stride_head = vm.stride(1);
+    s.vm_stride_token = vm.stride(2);
+  }
+  if (range[3] > range[2]) {
+    TORCH_CHECK(rk.defined() && rv.defined() && rk.dim() == 4 && rv.sizes() == rk.sizes() &&
+                    rk.size(1) == hkv && rk.size(3) == D && rk.size(2) >= range[3] &&
+                    rk.stride(3) == 1 && rv.stride(3) == 1 &&
+                    rk.scalar_type() == q.scalar_type() && rv.scalar_type() == q.scalar_type(),
+                "ckv::attention: residual must be [1,H,R,D] in the query dtype, last dim dense");
+    s.keys = rk.data_ptr();
+    s.rk_stride_head = rk.stride(1);
+    s.rk_stride_token = rk.stride(2);
+    s.values = rv.data_ptr();
+    s.rv_stride_head = rv.stride(1);
+    s.rv_stride_token = rv.stride(2);
+  }
+  return s;
+}
+
+// queries[i]: [1,Hq,nq,D]; banks and residuals per sequence; ranges[i*4..] =
+// (unit_begin, unit_end, resid_begin, resid_end).  Returns one tensor per
+// sequence: [1,Hq,nq,D] in the query dtype, or [Hq*nq, D+2] fp32 partials.
+std::vector<Tensor> attention(const std::vector<Tensor> &queries, const std::vector<Tensor> &kd,
+                              const std::vector<Tensor> &km, const std::vector<Tensor> &vd,
+                              const std::vector<Tensor> &vm, const std::vector<Tensor> &rk,
+                              const std::vector<Tensor> &rv, std::vector<int64_t> packed,
+                              std::vector<int64_t> lengths, std::vector<int64_t> ranges,
+                              int64_t bits, double scale, bool partial) {
+  const size_t n = queries.size();
+  TORCH_CHECK(n >= 1 && n <= CKV_MAX_SEQS, "ckv::attention: 1..", CKV_MAX_SEQS, " sequences per call");
+  TORCH_CHECK(kd.size() == n && km.size() == n && vd.size() == n && vm.size() == n &&
+                  rk.size() == n && rv.size() == n && packed.size() == n && lengths.size() == n &&
+                  ranges.size() == 4 * n,
+              "ckv::attention: per-sequence argument lists must have equal length");
+  const Tensor &q0 = queries[0];
+  require_cuda(q0, "query");
+  TORCH_CHECK(q0.dim() == 4 && q0.size(0) == 1 && q0.stride(3) == 1,
+              "ckv::attention: query must be [1,Hq,nq,D] with a dense last dim");
+  const int64_t hq = q0.size(1), nq = q0.size(2), D = q0.size(3);
+  int64_t hkv = 0;
+  for (size_t i = 0; i < n; ++i) {
+    if (ranges[4 * i + 1] > ranges[4 * i]) { hkv = kd[i].size(1); break; }
+    if (ranges[4 * i + 3] > ranges[4 * i + 2]) { hkv = rk[i].size(1); break; }
+  }
+  TORCH_CHECK(hkv > 0, "ckv::attention: every sequence range is empty");
+  c10::cuda::CUDAGuard guard(q0.device());
+  std::vector<ckv_seq> seqs(n);
+  std::vector<Tensor> outs(n);
+  for (size_t i = 0; i < n; ++i) {
+    const Tensor &q = queries[i];
+    TORCH_CHECK(q.device() == q0.device() && q.scalar_type() == q0.scalar_type() &&
+                    q.sizes() == q0.sizes() && q.stride(3) == 1,
+                "ckv::attention: queries must share device, dtype and shape");
+    for (const Tensor *t : {&kd[i], &km[i], &vd[i], &vm[i], &rk[i], &rv[i]})
+      TORCH_CHECK(!t->defined() || t->device() == q0.device(),
+                  "ckv::attention: all tensors must be on the query's device");
+    seqs[i] = make_seq(q, kd[i], km[i], vd[i], vm[i], rk[i], rv[i], packed[i], lengths[i],
+                       &ranges[4 * i], bits, hkv);
+    outs[i] = partial ? at::empty({hq * nq, D + 2}, q.options().dtype(at::kFloat))
+                      : at::empty({1, hq, nq, D}, q.options());
+    seqs[i].out = outs[i].data_ptr();
+  }
+  ckv_attn_args a{};
+  a.seqs = seqs.data();
+  a.num_seqs = int32_t(n);
+  a.heads_q = int32_t(hq);
+  a.heads_kv = int32_t(hkv);
+  a.head_dim = int32_t(D);
+  a.nq = int32_t(nq);
+  a.bits = int32_t(bits);
+  a.dtype = dtype_code(q0.scalar_type());
+  a.scale = float(scale);
+  a.partial = partial ? 1 : 0;
+  a.flags = CKV_WS_COUNTERS_ZERO;
+  size_t bytes = 0;
+  check_status(ckv_attention_workspace(&a, &bytes), "attention_workspace");
+  Tensor ws = workspace_for(q0, bytes);
+  check_status(ckv_attention(&a, ws.data_ptr(), size_t(ws.numel()), current_stream(q0)), "attention");
+  return outs;
+}
+
+Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
+  require_cuda(partials, "partials");
+  TORCH_CHECK(partials.dim() == 3 && partials.scalar_type() == at::kFloat,
+              "ckv::combine_partials: partials must be float32 [parts, rows, D+2]");
+  c10::cuda::CUDAGuard guard(partials.device());
+  Tensor p = partials.contiguous();
+  const int64_t parts = p.size(0), rows = p.size(1), D = p.size(2) - 2;
+  Tensor out = at::empty({rows, D}, p.options().dtype(dtype));
+  check_status(ckv_combine_partials(p.data_ptr<float>(), int(parts), rows, int(D), dtype_code(dtype),
+                                    out.data_ptr(), current_stream(p)),
+               "combine_partials");
+  return out;
+}
+
+}  // namespace
+
+TORCH_LIBRARY(ckv, m) {
+  m.def("pack_rows(Tensor rows, int bits, int rounding) -> (Tensor, Tensor)");
+  m.def("unpack_rows(Tensor data, Tensor meta, int bits, ScalarType dtype) -> Tensor");
+  m.def(
+      "pack_append(Tensor keys, Tensor values, Tensor(a!) key_data, Tensor(b!) key_meta, "
+      "Tensor(c!) value_data, Tensor(d!) value_meta, int count, int unit_offset, int bits, "
+      "int rounding) -> ()");
+  m.def(
+      "attention(Tensor[] queries, Tensor?[] key_data, Tensor?[] key_meta, Tensor?[] value_data, "
+      "Tensor?[] value_meta, Tensor?[] keys, Tensor?[] values, int[] packed, int[] lengths, "
+      "int[] ranges, int bits, float scale, bool partial) -> Tensor[]");
+  m.def("combine_partials(Tensor partials, ScalarType dtype) -> Tensor");
+}
+
+namespace {
+std::vector<Tensor> attention_opt(const std::vector<Tensor> &queries,
+                                  const c10::List<std::optional<Tensor>> &kd,
+                                  const c10::List<std::optional<Tensor>> &km,
+                                  const c10::List<std::optional<Tensor>> &vd,
+                                  const c10::List<std::optional<Tensor>> &vm,
+                                  const c10::List<std::optional<Tensor>> &rk,
+                                  const c10::List<std::optional<Tensor>> &rv,
+                                  std::vector<int64_t> packed, std::vector<int64_t> lengths,
+                                  std::vector<int64_t> ranges, int64_t bits, double scale,
+                                  bool partial) {
+  auto unwrap = [](const c10::List<std::optional<Tensor>> &l) {
+    std::vector<Tensor> v;
+    v.reserve(l.size());
+    for (size_t i = 0; i < l.size(); ++i) {
+      std::optional<Tensor> t = l.get(i);
+      v.push_back(t.has_value() ? *t : Tensor());
+    }
+    return v;
+  };
+  return attention(queries, unwrap(kd), unwrap(km), unwrap(vd), unwrap(vm), unwrap(rk), unwrap(rv),
+                   std::move(packed), std::move(lengths), std::move(ranges), bits, scale, partial);
+}
+}  // namespace
+
+TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
+  m.impl("pack_rows", &pack_rows);
+  m.impl("unpack_rows", &unpack_rows);
+  m.impl("pack_append", &pack_append);
+  m.impl("attention", &attention_opt);
+  m.impl("combine_partials", &combine_partials);
+}
