@@ -145,14 +145,22 @@ typedef struct {
   int32_t flags;                /* CKV_WS_COUNTERS_ZERO, ... */
 } ckv_attn_args;
 
-#define CKV_WS_COUNTERS_ZERO 1  /* caller guarantees the workspace counter
-                                   region is zero; the call leaves it zero */
+#define CKV_WS_COUNTERS_ZERO 1  /* caller guarantees the workspace header and
+                                   ticket region are zero; the call leaves the
+                                   tickets at zero */
 
-/* Maximum sequences in one ckv_attention call. */
-#define CKV_MAX_SEQS 96
+/* Maximum sequences in one ckv_attention call (the per-sequence descriptors,
+ * TMA tensor maps included, travel as kernel parameters). */
+#define CKV_MAX_SEQS 64
 
-/* Bytes of workspace ckv_attention needs for `args` (host-only, no CUDA). */
+/* Bytes of workspace ckv_attention needs for `args` (host only: reads the
+ * current device's SM count, launches nothing). */
 int ckv_attention_workspace(const ckv_attn_args *args, size_t *bytes);
+
+/* Copy the workspace's error word to *flag and wait for the stream: 0, or 1
+ * when a kernel gave up waiting for an asynchronous copy (about a second)
+ * instead of hanging.  The word stays set until the caller clears it. */
+int ckv_attention_error(const void *workspace, int *flag, ckv_stream_t stream);
 
 /*
  * Split-KV GQA attention over compressed views (decode when nq == 1,

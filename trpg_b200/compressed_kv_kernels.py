@@ -27,6 +27,8 @@ import torch
 
 from ._native import ops
 
+MAX_SEQS = 64   # CKV_MAX_SEQS in include/ckv.h
+
 
 def _inner_dense(t: torch.Tensor) -> torch.Tensor:
     """Banks need dense inner two dims and 16-byte aligned rows."""
@@ -34,6 +36,16 @@ def _inner_dense(t: torch.Tensor) -> torch.Tensor:
         t = t.contiguous()
     if t.data_ptr() % 16:
         t = t.clone(memory_format=torch.contiguous_format)
+    return t
+
+
+def _dense_rows(t: torch.Tensor) -> torch.Tensor:
+    """Value banks: each token's groups contiguous (TMA boxes / bulk copies of 32 tokens)."""
+    if (t.stride(-1) != 1 or t.stride(-2) != t.shape[-1]
+            or t.stride(-3) != t.shape[-2] * t.shape[-1] or t.data_ptr() % 16):
+        t = t.contiguous()
+        if t.data_ptr() % 16:
+            t = t.clone()
     return t
 
 
@@ -69,26 +81,40 @@ def attention(queries: Sequence[torch.Tensor], views: Sequence, scale: float, *,
         has_packed = rng[1] > rng[0]
         kd.append(_inner_dense(v.key_data) if has_packed else None)
         km.append(_inner_dense(v.key_meta) if has_packed else None)
-        vd.append(_inner_dense(v.value_data) if has_packed else None)
-        vm.append(_inner_dense(v.value_meta) if has_packed else None)
+        vd.append(_dense_rows(v.value_data) if has_packed else None)
+        vm.append(_dense_rows(v.value_meta) if has_packed else None)
         has_resid = rng[3] > rng[2]
         rk.append(_residual(v.keys) if has_resid else None)
         rv.append(_residual(v.values) if has_resid else None)
         packed.append(int(v.packed_tokens))
         lengths.append(int(v.length))
         flat.extend(int(x) for x in rng)
-    return ops().attention(list(queries), kd, km, vd, vm, rk, rv, packed, lengths, flat, int(bits),
-                           float(scale), bool(partial))
+    out = []
+    for c in range(0, len(queries), MAX_SEQS):      # the kernel takes 64 sequences per launch
+        sl = slice(c, c + MAX_SEQS)
+        out += ops().attention(list(queries[sl]), kd[sl], km[sl], vd[sl], vm[sl], rk[sl], rv[sl],
+                               packed[sl], lengths[sl], flat[4 * c:4 * (c + MAX_SEQS)], int(bits),
+                               float(scale), bool(partial))
+    return out
+
+
+def _single(query, view, scale):
+    if view.packed_tokens < 128 or view.keys.shape[2] == 0:
+        return attention([query], [view], scale)[0]
+    return ops().decode(query, _inner_dense(view.key_data), _inner_dense(view.key_meta),
+                        _dense_rows(view.value_data), _dense_rows(view.value_meta),
+                        _residual(view.keys), _residual(view.values), int(view.packed_tokens),
+                        int(view.length), int(view.bits), float(scale))
 
 
 def decode(query: torch.Tensor, view, scale: float) -> torch.Tensor:
     """Single-query GQA decode over a packed view (``compressed_kv_kernels.py:93``)."""
-    return attention([query], [view], scale)[0]
+    return _single(query, view, scale)
 
 
 def verify(query: torch.Tensor, view, scale: float) -> torch.Tensor:
     """Multi-query verify: lower-right causal attention of query [1,Hq,n,D]."""
-    return attention([query], [view], scale)[0]
+    return _single(query, view, scale)
 
 
 def combine(partials: Sequence[torch.Tensor] | torch.Tensor, dtype: torch.dtype) -> torch.Tensor:

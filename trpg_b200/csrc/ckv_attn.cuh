@@ -2,9 +2,12 @@
 //
 // One launch covers every (sequence, KV head) pair of a call.  Each pair is
 // split across `cph` CTAs; each CTA splits its share across WARPS warps; each
-// warp streams its own work items through a private two-slot cp.async ring
-// and keeps its own online-softmax state.  Warps merge inside the CTA, CTAs
-// merge in the last CTA of the pair (atomic ticket), all in one launch.
+// warp streams its own work items through a private two-slot ring in shared
+// memory and keeps its own online-softmax state.  Packed tiles arrive by TMA
+// (cp.async.bulk.tensor from per-sequence tensor maps, metadata by 1-D bulk
+// copies) signalled on one mbarrier per slot; the exact residual arrives by
+// 16-byte cp.async.  Warps merge inside the CTA, CTAs merge in the last CTA of
+// the pair (atomic ticket), all in one launch.
 //
 // Work items:
 //   packed block  -- 128 tokens of one KV head, consumed in "quarters" of
@@ -29,10 +32,14 @@
 //   * K slot rows are channels (32 bytes each); A-fragment k-index 2qd+e
 //     maps to channel 16s+qd+4e', so the four lanes of a row group read rows
 //     8 words apart.
-//   * V slot rows are tokens with a pitch of 8 (mod 32) words; the PV k-index
-//     maps to token qd+4e so the four lane groups land in different banks.
+//   * V slot rows are tokens, loaded as 128-byte boxes with the TMA 128-byte
+//     swizzle (16-byte chunk c of row t lands at chunk c ^ (t & 7)); with the
+//     natural PV token order (k-index 2qd+b <-> token 2qd+b) the 8 lanes of a
+//     quarter-warp read 8 different chunks.
 //   * P is stored permuted so each lane's B fragment is one 8-byte load.
 #pragma once
+
+#include <cuda.h>
 
 #include "ckv_common.cuh"
 
@@ -42,35 +49,42 @@ namespace attn {
 constexpr int WARPS = 8;
 constexpr int THREADS = WARPS * 32;
 constexpr int PPITCH = 160;          // bytes per P row (<= 64 tokens), 40 words
-constexpr int VM_PLANE = 32 * 8 + 32; // bytes per value-meta plane (32 tokens)
 
-struct SeqDev {
+struct alignas(64) SeqDev {
+  CUtensorMap tk;   // key codes   [H][units][D][S] bytes, box 32 bytes x D channels
+  CUtensorMap tv;   // value codes [H][tokens][D*bits/8] bytes, box VBOX bytes x 32 tokens
   const void *q;
-  const uint8_t *kd;
   const float *km;
-  const uint8_t *vd;
   const float *vm;
   const void *rk;
   const void *rv;
   void *out;
   int64_t q_h, q_n;
-  int64_t kd_h, kd_u, km_h, km_u;
-  int64_t vd_h, vd_t, vm_h, vm_t;
+  int64_t km_h, km_u, vm_h, vm_t;
   int64_t rk_h, rk_t, rv_h, rv_t;
   int32_t packed, length;
   int32_t ub, ue, rb, re;
   int32_t cta_begin, cph;
 };
 
-struct Params {
+struct ParamsHead {
   int32_t num_seqs, hkv, group, nq, rows;
   int32_t partial;
   float scale_log2;
   float *rec;           // [grid][rows][D]
   float *rec_ml;        // [grid][rows][2]
   unsigned *counters;   // [num_seqs * hkv]
-  SeqDev seq[CKV_MAX_SEQS];
+  unsigned *error;      // set to 1 when a wait gives up
 };
+
+// Kernel parameters: a single-sequence call passes a ~300-byte block, a
+// batched call the full table (launch cost grows with parameter size).
+template <int MAXS>
+struct alignas(64) Params : ParamsHead {
+  SeqDev seq[MAXS];
+};
+
+constexpr int kMaxCph = 256;  // CTAs per (sequence, KV head), bounded by the merge scratch
 
 template <int BITS, int D, int NT>
 struct Cfg {
@@ -81,32 +95,47 @@ struct Cfg {
   static constexpr int MTQ = QT / 16;                   // m-tiles per K slot
   static constexpr int VSQ = QT / 32;                   // V slots per K slot
   static constexpr int SPB = QPB * (1 + VSQ);           // slots per packed block
-  static constexpr int KSLOT = D * 32;                  // K slot bytes
+  static constexpr int KSLOT = D * 32;                  // K slot bytes (TMA box 32 B x D)
+  static constexpr int KMETA = D * 8;                   // key (scale, low) of one block
   static constexpr int VROWB = D * BITS / 8;            // bytes of one token's value codes
-  static constexpr int VPITCH = VROWB + 32 > 96 ? VROWB + 32 : 96;
+  static constexpr int VBOX = VROWB < 128 ? VROWB : 128; // TMA box width (bytes)
+  static constexpr int NVB = VROWB / VBOX;              // boxes per value slot
+  static constexpr int VSWZ = VBOX == 128 ? 7 : (VBOX == 64 ? 3 : 1);  // swizzle row mask
   static constexpr int NG = D / 64;
-  static constexpr int VSLOT = 32 * VPITCH + NG * VM_PLANE;
+  static constexpr int VMETA = 32 * NG * 8;             // value (scale, low) of 32 tokens
+  static constexpr int VSLOT = 32 * VROWB + VMETA;
   // Value lane mapping: lane r owns CPL channels in each of NCH chunks.
   static constexpr int CPL = BITS == 8 ? (D >= 128 ? 16 : 8) : D / 8;
   static constexpr int NCH = D / (8 * CPL);
   static constexpr int MTC = CPL / 2;                   // m-tiles per chunk
   static constexpr int MTV = D / 16;                    // m-tiles of the output
-  // Residual slots (16 tokens of 16-bit values).
+  // Residual slots (16 tokens of 16-bit values, padded pitch, cp.async).
   static constexpr int RKP = 2 * D + 32;
   static constexpr int RVP = CPL == 8 ? 2 * D + 32 : 2 * D + 16;
   static constexpr int RSLOT_K = 16 * RKP;
   static constexpr int RSLOT_V = 16 * RVP;
   static constexpr int SLOT_RAW = KSLOT > VSLOT ? KSLOT : VSLOT;
   static constexpr int SLOT_R = RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V;
-  static constexpr int SLOT = ((SLOT_RAW > SLOT_R ? SLOT_RAW : SLOT_R) + 127) / 128 * 128;
-  static constexpr int KMETA = D * 8;
+  // Slots start on 1024-byte boundaries (required by the 128-byte swizzle).
+  static constexpr int SLOT = ((SLOT_RAW > SLOT_R ? SLOT_RAW : SLOT_R) + 1023) / 1024 * 1024;
   static constexpr int PBUF = 8 * NT * PPITCH;
-  static constexpr int WARP_BYTES = 2 * SLOT + KMETA + PBUF;
+  static constexpr int WARP_BYTES = (2 * SLOT + KMETA + PBUF + 1023) / 1024 * 1024;
   static constexpr int QFRAG = KSTEPS * NT * 32 * 8;    // one fragment set
-  static constexpr int SMEM = 2 * QFRAG + WARPS * WARP_BYTES;
+  static constexpr int QFRAG_AL = (2 * QFRAG + 1023) / 1024 * 1024;
+  static constexpr int SMEM = 1024 + QFRAG_AL + WARPS * WARP_BYTES;  // + alignment slack
   static constexpr int MERGE = WARPS * 8 * NT * (D + 2) * 4;
   static_assert(MERGE <= WARPS * WARP_BYTES, "merge scratch must fit the warp region");
+  static_assert(2 * 16 * 256 * 4 + 16 * 2 * 4 <= WARPS * WARP_BYTES,
+                "final-merge scratch (rows x CTAs per pair) must fit the warp region");
 };
+
+// Offset of byte `a` of a TMA box (rows of 128/64/32 bytes) after the hardware
+// swizzle: 16-byte chunk bits [4,7) XOR row bits [7,10) (128 B), [4,6) with
+// [7,9) (64 B), bit 4 with bit 7 (32 B).
+template <int MASK>
+__device__ __forceinline__ uint32_t swz(uint32_t a) {
+  return a ^ (((a >> 7) & MASK) << 4);
+}
 
 // Residual PV token order: k-index (qd, e) -> token A[qd] + B[e].
 template <int CPL>
@@ -128,10 +157,11 @@ __device__ __forceinline__ int resid_pos(int t) {
     return 4 * (t & 3) + (t >> 2);
   }
 }
-// Position of packed token t (0..63) in the permuted P row.
+// Position of packed token t (0..63) in the permuted P row: within each
+// 16-token k-step, lane qd's four tokens 2qd, 2qd+1, 2qd+8, 2qd+9 sit at
+// 4qd..4qd+3 so its B fragment is one 8-byte load.
 __device__ __forceinline__ int packed_pos(int t) {
-  int w = t & 15;
-  return (t & ~15) | ((w & 3) << 2) | (w >> 2);
+  return (t & ~15) | (((t & 7) >> 1) << 2) | (((t >> 3) & 1) << 1) | (t & 1);
 }
 
 template <int BITS, int D, int NT, int DT>
@@ -176,38 +206,26 @@ struct Warp {
   }
 
   // ---------------------------------------------------------------------
-  // Slot loads (every lane issues its share of 16-byte async copies)
+  // Packed slot loads: lane 0 issues TMA tile copies (+ 1-D bulk copies of
+  // the metadata) that complete on the slot's mbarrier.
   // ---------------------------------------------------------------------
   __device__ void load_packed_k(const SeqDev &sd, int head, int unit, int quarter, uint32_t slot,
-                                bool with_meta) {
-    const uint8_t *src = sd.kd + head * sd.kd_h + int64_t(unit) * sd.kd_u;
-    constexpr int ROWB = 128 * BITS / 8;  // bytes per channel row of the bank
-#pragma unroll 4
-    for (int x = lane; x < 2 * D; x += 32) {
-      const int c = x >> 1, half = x & 1;
-      cp_async16(slot + c * 32 + half * 16, src + c * ROWB + quarter * 32 + half * 16);
-    }
-    if (with_meta) {
-      const float *msrc = sd.km + head * sd.km_h + int64_t(unit) * sd.km_u;
-#pragma unroll
-      for (int x = lane; x < D / 2; x += 32) cp_async16(kmeta + x * 16, msrc + x * 4);
+                                bool with_meta, uint32_t bar) {
+    if (lane == 0) {
+      mbar_expect_tx(bar, C::KSLOT + (with_meta ? C::KMETA : 0));
+      tma_load_4d(slot, &sd.tk, bar, quarter * 32, 0, unit, head);
+      if (with_meta)
+        bulk_load(kmeta, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, bar);
     }
   }
 
-  __device__ void load_packed_v(const SeqDev &sd, int head, int64_t tok0, uint32_t slot) {
-    const uint8_t *src = sd.vd + head * sd.vd_h + tok0 * sd.vd_t;
-    constexpr int CH = C::VROWB / 16;  // 16-byte chunks per token row
-#pragma unroll 4
-    for (int x = lane; x < 32 * CH; x += 32) {
-      const int t = x / CH, k = x % CH;
-      cp_async16(slot + t * C::VPITCH + k * 16, src + t * sd.vd_t + k * 16);
-    }
-    const float *msrc = sd.vm + head * sd.vm_h + tok0 * sd.vm_t;
-    const uint32_t mdst = slot + 32 * C::VPITCH;
+  __device__ void load_packed_v(const SeqDev &sd, int head, int tok0, uint32_t slot, uint32_t bar) {
+    if (lane == 0) {
+      mbar_expect_tx(bar, C::VSLOT);
 #pragma unroll
-    for (int x = lane; x < 32 * C::NG; x += 32) {
-      const int t = x / C::NG, g = x % C::NG;
-      cp_async8(mdst + g * VM_PLANE + t * 8, msrc + t * sd.vm_t + g * 2);
+      for (int bx = 0; bx < C::NVB; ++bx)
+        tma_load_3d(slot + bx * 32 * C::VBOX, &sd.tv, bar, bx * C::VBOX, tok0, head);
+      bulk_load(slot + 32 * C::VROWB, sd.vm + head * sd.vm_h + int64_t(tok0) * sd.vm_t, C::VMETA, bar);
     }
   }
 
@@ -376,7 +394,7 @@ struct Warp {
   // slot within the current K slot's P row.
   // ---------------------------------------------------------------------
   __device__ void pv_packed(uint32_t slot, int kbase) {
-    const uint32_t meta = slot + 32 * C::VPITCH;
+    const uint32_t meta = slot + 32 * C::VROWB;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       uint2 b[NT];
@@ -392,8 +410,11 @@ struct Warp {
         float2 sc[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int t = 16 * j + qd + 4 * e;
-          const uint32_t addr = slot + t * C::VPITCH + c0 * BITS / 8;
+          // k-index 2qd, 2qd+1, 2qd+8, 2qd+9 <-> slot token 16j + the same
+          const int t = 16 * j + 2 * qd + (e & 1) + 8 * (e >> 1);
+          const int off = c0 * BITS / 8;                 // byte of the lane's chunk in the row
+          const uint32_t addr = slot + (off / C::VBOX) * 32 * C::VBOX +
+                                swz<C::VSWZ>(t * C::VBOX + off % C::VBOX);
           if constexpr (CB == 16) {
             uint4 v = lds128(addr);
             w[e][0] = v.x; w[e][1] = v.y; w[e][2] = v.z; w[e][3] = v.w;
@@ -403,7 +424,7 @@ struct Warp {
           } else {
             w[e][0] = lds32(addr);
           }
-          const float2 sm = lds64f(meta + grp * VM_PLANE + t * 8);
+          const float2 sm = lds64f(meta + (t * C::NG + grp) * 8);
           sc[e] = make_float2(sm.x, sm.x);
           lo[e] = make_float2(sm.y, sm.y);
         }

@@ -240,6 +240,9 @@ ckv_seq make_seq(const Tensor &q, const Tensor &kd, const Tensor &km, const Tens
   return s;
 }
 
+void run_attention(std::vector<ckv_seq> &seqs, const Tensor &q0, int64_t hq, int64_t hkv, int64_t D,
+                   int64_t nq, int64_t bits, double scale, bool partial);
+
 // queries[i]: [1,Hq,nq,D]; banks and residuals per sequence; ranges[i*4..] =
 // (unit_begin, unit_end, resid_begin, resid_end).  Returns one tensor per
 // sequence: [1,Hq,nq,D] in the query dtype, or [Hq*nq, D+2] fp32 partials.
@@ -283,6 +286,13 @@ std::vector<Tensor> attention(const std::vector<Tensor> &queries, const std::vec
                       : at::empty({1, hq, nq, D}, q.options());
     seqs[i].out = outs[i].data_ptr();
   }
+  run_attention(seqs, q0, hq, hkv, D, nq, bits, scale, partial);
+  return outs;
+}
+
+void run_attention(std::vector<ckv_seq> &seqs, const Tensor &q0, int64_t hq, int64_t hkv, int64_t D,
+                   int64_t nq, int64_t bits, double scale, bool partial) {
+  const size_t n = seqs.size();
   ckv_attn_args a{};
   a.seqs = seqs.data();
   a.num_seqs = int32_t(n);
@@ -299,7 +309,26 @@ std::vector<Tensor> attention(const std::vector<Tensor> &queries, const std::vec
   check_status(ckv_attention_workspace(&a, &bytes), "attention_workspace");
   Tensor ws = workspace_for(q0, bytes);
   check_status(ckv_attention(&a, ws.data_ptr(), size_t(ws.numel()), current_stream(q0)), "attention");
-  return outs;
+}
+
+// Single sequence, plain tensors: the decode / verify fast path.
+Tensor decode(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor &vd,
+              const Tensor &vm, const Tensor &rk, const Tensor &rv, int64_t packed, int64_t length,
+              int64_t bits, double scale) {
+  require_cuda(q, "query");
+  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1 && q.stride(3) == 1,
+              "ckv::decode: query must be [1,Hq,nq,D] with a dense last dim");
+  for (const Tensor *t : {&kd, &km, &vd, &vm, &rk, &rv})
+    TORCH_CHECK(t->device() == q.device(), "ckv::decode: all tensors must be on the query's device");
+  c10::cuda::CUDAGuard guard(q.device());
+  const int64_t range[4] = {0, packed / 128, 0, rk.size(2)};
+  const int64_t hkv = rk.size(1);
+  std::vector<ckv_seq> seqs(1);
+  seqs[0] = make_seq(q, kd, km, vd, vm, rk, rv, packed, length, range, bits, hkv);
+  Tensor out = at::empty_like(q, at::MemoryFormat::Contiguous);
+  seqs[0].out = out.data_ptr();
+  run_attention(seqs, q, q.size(1), hkv, q.size(3), q.size(2), bits, scale, false);
+  return out;
 }
 
 Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
@@ -330,6 +359,9 @@ TORCH_LIBRARY(ckv, m) {
       "Tensor?[] value_meta, Tensor?[] keys, Tensor?[] values, int[] packed, int[] lengths, "
       "int[] ranges, int bits, float scale, bool partial) -> Tensor[]");
   m.def("combine_partials(Tensor partials, ScalarType dtype) -> Tensor");
+  m.def(
+      "decode(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
+      "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
 }
 
 namespace {
@@ -363,4 +395,5 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("pack_append", &pack_append);
   m.impl("attention", &attention_opt);
   m.impl("combine_partials", &combine_partials);
+  m.impl("decode", &decode);
 }
