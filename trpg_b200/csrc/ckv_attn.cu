@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   using T = typename Elem<DT>::T;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int s_seq, s_last;
-  __shared__ __align__(8) uint64_t s_bar[WARPS][2];
+  __shared__ __align__(8) uint64_t s_bar[WARPS][RING];
   // 1024-byte aligned base: the 128-byte TMA swizzle needs aligned slots.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
@@ -48,35 +48,14 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const int head = local / sd.cph, split = local % sd.cph;
   const int G = p.group, rows = p.rows, nq = p.nq;
 
-  // ---- query fragments for both channel orders -----------------------------
-  const uint32_t qfp = smem_u32(smem), qfr = qfp + C::QFRAG;
-  const uint32_t bar0 = smem_u32(&s_bar[warp][0]), bar1 = smem_u32(&s_bar[warp][1]);
+  // ---- query fragments (MMA B operand, k-index 2qd+b <-> channel 2qd+b) ----
+  const uint32_t qf = smem_u32(smem);
+  const uint32_t bar_base = smem_u32(&s_bar[warp][0]);
   if (lane == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar1, 1);
+#pragma unroll
+    for (int k = 0; k < RING; ++k) mbar_init(bar_base + 8 * k, 1);
     mbar_fence_init();
   }
-  {
-    const uint16_t *q = static_cast<const uint16_t *>(sd.q);
-    for (int x = tid; x < C::KSTEPS * NT * 32; x += THREADS) {
-      const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
-      const int rr = ln >> 2, qq = ln & 3, row = 8 * nt + rr;
-      uint2 vp = make_uint2(0, 0), vr = make_uint2(0, 0);
-      if (row < rows) {
-        const int n = row / G, g = row % G;
-        const uint16_t *qrow = q + (head * G + g) * sd.q_h + n * sd.q_n;
-        const int cp = 16 * s + qq, cr = 16 * s + 4 * qq;
-        vp.x = qrow[cp] | (uint32_t(qrow[cp + 4]) << 16);
-        vp.y = qrow[cp + 8] | (uint32_t(qrow[cp + 12]) << 16);
-        vr.x = qrow[cr] | (uint32_t(qrow[cr + 1]) << 16);
-        vr.y = qrow[cr + 2] | (uint32_t(qrow[cr + 3]) << 16);
-      }
-      *reinterpret_cast<uint2 *>(smem + x * 8) = vp;
-      *reinterpret_cast<uint2 *>(smem + C::QFRAG + x * 8) = vr;
-    }
-  }
-  __syncthreads();
-
   // ---- this warp's work items ---------------------------------------------
   const int np = sd.ue - sd.ub;
   const int nr = (sd.re - sd.rb + 15) / 16;
@@ -87,101 +66,123 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const int kt = ie > first ? (ie - first + WARPS - 1) / WARPS : 0;
   const int pend = ie < np ? ie : np;
   const int kp = pend > first ? (pend - first + WARPS - 1) / WARPS : 0;
-  const int total = kp * C::SPB + (kt - kp) * 2;
+  const int total = kp * C::SPB + (kt - kp) * 4;
 
   Warp<BITS, D, NT, DT> w;
-  w.init(lane, qfp, qfr, qfp + C::QFRAG_AL + warp * C::WARP_BYTES, p.scale_log2);
+  w.init(lane, qf, qf + C::QFRAG_AL + warp * C::WARP_BYTES, p.scale_log2);
 
   const T *rk = static_cast<const T *>(sd.rk) + head * sd.rk_h;
   const T *rv = static_cast<const T *>(sd.rv) + head * sd.rv_h;
   const int length = sd.length, packed = sd.packed;
 
   auto is_tma = [&](int s) { return s < kp * C::SPB; };
+  auto bar_of = [&](int s) { return bar_base + 8 * (s % RING); };
   auto issue = [&](int s) {
-    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
-    const uint32_t bar = (s & 1) ? bar1 : bar0;
+    const uint32_t slot = w.ring + (s % RING) * C::SLOT;
     if (is_tma(s)) {
       const int k = s / C::SPB, part = s % C::SPB;
       const int unit = sd.ub + first + k * WARPS;
-      const int qq = part / (1 + C::VSQ), sub = part % (1 + C::VSQ);
-      if (sub == 0)
-        w.load_packed_k(sd, head, unit, qq, slot, qq == 0, bar);
+      if (part < C::KS)
+        w.load_packed_k(sd, head, unit, part, slot, bar_of(s));
       else
-        w.load_packed_v(sd, head, unit * 128 + qq * C::QT + (sub - 1) * 32, slot, bar);
+        w.load_packed_v(sd, head, unit * 128 + (part - C::KS) * C::VT, slot, bar_of(s));
     } else {
-      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
+      const int k = (s - kp * C::SPB) >> 2, part = (s - kp * C::SPB) & 3;
       const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
-      if (part == 0)
-        w.load_resid(rk, sd.rk_t, t0, sd.re, slot, C::RKP);
+      if (part < 2)
+        w.load_resid(rk, sd.rk_t, t0, sd.re, 16, part * (D / 2), D / 2, slot, C::RKP);
       else
-        w.load_resid(rv, sd.rv_t, t0, sd.re, slot, C::RVP);
+        w.load_resid(rv, sd.rv_t, t0 + 8 * (part - 2), sd.re, 8, 0, D, slot, C::RVP);
     }
   };
 
   const int rr = lane >> 2;
   auto compute = [&](int s) {
-    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
+    const uint32_t slot = w.ring + (s % RING) * C::SLOT;
     if (is_tma(s)) {
       const int part = s % C::SPB;
-      const int sub = part % (1 + C::VSQ);
-      if (sub == 0) {
-        w.qk_packed(slot);
-        w.template softmax<C::MTQ>(
-            [&](int mt, int h) { return C::TPL * rr + 2 * mt + h; },
-            [](int, int) { return true; }, [](int t) { return packed_pos(t); });
+      if (part < C::KS) {
+        if (part == 0) w.zero_s();
+        w.qk_packed(slot, part);
+        if (part == C::KS - 1)
+          w.template softmax<8>([&](int mt, int h) { return 16 * rr + 2 * mt + h; },
+                                [](int, int) { return true; }, [](int t) { return packed_pos(t); });
       } else {
-        w.pv_packed(slot, 2 * (sub - 1));
+        w.pv_packed(slot, part - C::KS);
       }
     } else {
-      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
-      if (part == 0) {
-        const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
-        w.qk_resid(slot);
-        w.template softmax<1>(
-            [&](int, int h) { return rr + 8 * h; },
-            [&](int t, int row) {
-              const int ri = t0 + t;
-              return ri < sd.re && (nq == 1 || packed + ri <= length - nq + row / G);
-            },
-            [](int t) { return resid_pos<C::CPL>(t); });
+      const int k = (s - kp * C::SPB) >> 2, part = (s - kp * C::SPB) & 3;
+      if (part < 2) {
+        if (part == 0) w.zero_s();
+        w.qk_resid(slot, part);
+        if (part == 1) {
+          const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
+          w.template softmax<1>(
+              [&](int, int h) { return rr + 8 * h; },
+              [&](int t, int row) {
+                const int ri = t0 + t;
+                return ri < sd.re && (nq == 1 || packed + ri <= length - nq + row / G);
+              },
+              [](int t) { return resid_pos<C::CPL>(t); });
+        }
       } else {
-        w.pv_resid(slot);
+        w.pv_resid(slot, part - 2);
       }
     }
   };
 
-  // Every slot commits one cp.async group (empty for TMA slots), so the
-  // residual slots can wait with cp.async.wait_group 1; TMA slots wait on
-  // their mbarrier phase.
+  // Every slot commits one cp.async group (empty for TMA slots), so residual
+  // slots wait with cp.async.wait_group RING-2; TMA slots wait on the phase
+  // of their ring slot's mbarrier.
   uint32_t phase = 0;  // bit k: parity of the next completion of ring slot k
   __syncwarp();
-  if (total > 0) issue(0);
-  cp_async_commit();
-  if (total > 1) issue(1);
-  cp_async_commit();
+#pragma unroll
+  for (int k = 0; k < RING - 1; ++k) {
+    if (k < total) issue(k);
+    cp_async_commit();
+  }
+  // Query fragments are built while the first slots are in flight.
+  {
+    const uint16_t *q = static_cast<const uint16_t *>(sd.q);
+    for (int x = tid; x < C::KSTEPS * NT * 32; x += THREADS) {
+      const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
+      const int rr = ln >> 2, qq = ln & 3, row = 8 * nt + rr;
+      uint2 v = make_uint2(0, 0);
+      if (row < rows) {
+        const int n = row / G, g = row % G;
+        const uint16_t *qrow = q + (head * G + g) * sd.q_h + n * sd.q_n;
+        const int c = 16 * s + 2 * qq;
+        v.x = qrow[c] | (uint32_t(qrow[c + 1]) << 16);
+        v.y = qrow[c + 8] | (uint32_t(qrow[c + 9]) << 16);
+      }
+      *reinterpret_cast<uint2 *>(smem + x * 8) = v;
+    }
+  }
+  __syncthreads();
+
   int s = 0;
   for (; s < total; ++s) {
+    const int k = s % RING;
     if (is_tma(s)) {
-      const int k = s & 1;
-      if (!mbar_wait(k ? bar1 : bar0, (phase >> k) & 1)) {
+      if (!mbar_wait(bar_of(s), (phase >> k) & 1)) {
         if (lane == 0) atomicOr(p.error, 1u);
         break;
       }
       phase ^= 1u << k;
     } else {
-      cp_async_wait<1>();
+      cp_async_wait<RING - 2>();
     }
     __syncwarp();
     compute(s);
     __syncwarp();
-    if (s + 2 < total) issue(s + 2);
+    if (s + RING - 1 < total) issue(s + RING - 1);
     cp_async_commit();
   }
   if (s < total) {
     // A wait gave up: let the copies still in flight land (bounded) before
     // this CTA's shared memory is reused or released.
-    for (int k2 = s; k2 < s + 2 && k2 < total; ++k2)
-      if (is_tma(k2)) mbar_wait((k2 & 1) ? bar1 : bar0, (phase >> (k2 & 1)) & 1);
+    for (int k2 = s; k2 < s + RING - 1 && k2 < total; ++k2)
+      if (is_tma(k2)) mbar_wait(bar_of(k2), (phase >> (k2 % RING)) & 1);
   }
   cp_async_wait<0>();
 
@@ -491,13 +492,14 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
     set_last_error("cuTensorMapEncodeTiled unavailable");
     return CKV_ERR_CUDA;
   }
-  constexpr uint64_t S = 128 * BITS / 8;
+  constexpr uint64_t S = C::S;
   const cuuint64_t kdims[4] = {S, cuuint64_t(D), cuuint64_t(s.unit_end), cuuint64_t(hkv)};
   const cuuint64_t kstr[3] = {S, cuuint64_t(s.kd_stride_unit), cuuint64_t(s.kd_stride_head)};
-  const cuuint32_t kbox[4] = {32, cuuint32_t(D), 1, 1};
+  const cuuint32_t kbox[4] = {cuuint32_t(S), cuuint32_t(C::KCH), 1, 1};
   const cuuint32_t one[4] = {1, 1, 1, 1};
   CUresult r = enc(&d.tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(s.key_data), kdims,
-                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   S == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("key tensor map rejected (bank strides)");
@@ -505,7 +507,7 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   }
   const cuuint64_t vdims[3] = {cuuint64_t(C::VROWB), cuuint64_t(s.unit_end) * 128, cuuint64_t(hkv)};
   const cuuint64_t vstr[2] = {cuuint64_t(s.vd_stride_token), cuuint64_t(s.vd_stride_head)};
-  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), 32, 1};
+  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), cuuint32_t(C::VT), 1};
   const CUtensorMapSwizzle swz = C::VBOX == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : C::VBOX == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
