@@ -1,22 +1,22 @@
 // Split-KV GQA attention over the compressed KV cache (sm_100a).
 //
 // One launch covers every (sequence, KV head) pair of a call.  Each pair is
-// split across `cph` CTAs; each CTA splits its share across WARPS warps; each
-// warp streams its own work items through a private RING-slot ring in shared
-// memory and keeps its own online-softmax state.  Packed tiles arrive by TMA
-// (cp.async.bulk.tensor from per-sequence tensor maps, metadata by 1-D bulk
-// copies) and signal one mbarrier per ring slot; the exact residual window
-// arrives by 16-byte cp.async.  Warps merge inside the CTA, CTAs merge in the
-// last CTA of the pair (atomic ticket), all in one launch.
-//
-// Work items and the slots they stream:
-//   packed block  -- 128 tokens of one KV head: KS key slots (KC channels x
-//                    all 128 tokens each, one TMA box of 128-token rows), then
-//                    8 value slots (16 tokens x all channels).  QK^T
-//                    accumulates over the key slots; the online softmax runs
-//                    once per block; P.V runs per value slot.
-//   residual item -- 16 exact tokens: two key slots (channel halves) and two
-//                    value slots (token halves).
+// split across `cph` CTAs.  A CTA holds NCW warps in groups of GW:
+//   * packed blocks (128 tokens) go to groups; the GW warps of a group split
+//     a block's tokens into columns of TPW = 128/GW tokens.  Key slots (KCH
+//     channels x 128 tokens, one TMA box of 128-token rows) are shared by the
+//     group: the group's first warp streams them through the group's RK-slot
+//     ring (full/empty mbarriers), RK-1 slots ahead of its own consumption.
+//     Each warp streams its own value slots (16 tokens x all channels) and
+//     residual slots through a private RV-slot ring;
+//   * residual items (16 exact tokens) go to single consumer warps;
+//   * every consumer warp keeps its own online-softmax state; warps merge
+//     inside the CTA, CTAs merge in the last CTA of the pair (atomic ticket),
+//     all in one launch.
+// Packed tiles arrive by TMA (cp.async.bulk.tensor from per-sequence tensor
+// maps, metadata by 1-D bulk copies); the exact residual by 16-byte
+// cp.async.  Every wait on a barrier is bounded (about a second) and flags an
+// error instead of hanging.
 //
 // Numerics follow models/compressed_kv_kernels.py:_partial (:12-77): a code
 // is dequantized as fma(code, scale, low) and rounded to the query dtype
@@ -34,8 +34,8 @@
 // is free, so rows (M) are permuted instead:
 //   * key slot rows are channels of 128 (Q8) or 64 (Q4) bytes, loaded with
 //     the TMA 128/64-byte swizzle (16-byte chunk c of row y lands at c ^ f(y));
-//     lane r owns tokens 16r..16r+15 (one 16- or 8-byte load per channel)
-//     and the 8 lanes of a quarter-warp hit 8 different chunks;
+//     in its column, lane r owns tokens TPL*r .. TPL*r+TPL-1 (one 4-byte
+//     load per channel); for Q8 the 32 lanes hit 32 different banks;
 //   * value slot rows are tokens, loaded as 128-byte swizzled boxes; lane r
 //     owns CPL channels per chunk;
 //   * P is stored permuted so each lane's B fragment is one 8-byte load.
@@ -48,16 +48,12 @@
 namespace ckv {
 namespace attn {
 
-#ifndef CKV_WARPS
-#define CKV_WARPS 8
-#endif
-#ifndef CKV_RING
-#define CKV_RING 4
-#endif
-constexpr int WARPS = CKV_WARPS;     // warps per CTA (one CTA per SM)
-constexpr int THREADS = WARPS * 32;
-constexpr int RING = CKV_RING;       // slots per warp
-constexpr int PPITCH = 288;          // bytes per P row (128 tokens + pad), 72 words
+constexpr int NCW = 8;               // consumer warps per CTA (one CTA per SM)
+constexpr int WARPS = NCW;           // warps holding softmax state
+constexpr int THREADS = NCW * 32;
+constexpr int RKMAX = 4;             // key slots per group ring (at most)
+constexpr int RV = 3;                // value / residual slots per consumer ring
+constexpr int PPITCH = 160;          // bytes per P row (<= 64 tokens + pad), 40 words
 
 struct alignas(64) SeqDev {
   CUtensorMap tk;   // key codes   [H][units][D][S] bytes; box S bytes x KC channels
@@ -105,9 +101,14 @@ struct Cfg {
   static constexpr int KSLOT = KCH * S;                  // key slot bytes
   static constexpr int KSWZ = S == 128 ? 7 : 3;          // key swizzle row mask (128 / 64 B)
   static constexpr int KMETA = D * 8;                    // key (scale, low) of one block
+  static constexpr int GW = BITS == 8 ? 4 : 2;           // consumer warps per group
+  static constexpr int RK = GW == 4 ? RKMAX : 3;         // key slots per group ring
+  static constexpr int NGRP = NCW / GW;                  // groups per CTA
+  static constexpr int TPW = 128 / GW;                   // tokens per warp column
+  static constexpr int TPL = TPW / 8;                    // tokens per lane (4 B of codes)
+  static constexpr int MTW = TPW / 16;                   // m-tiles per column
   static constexpr int VT = 16;                          // tokens per value slot
-  static constexpr int NVS = 128 / VT;                   // value slots per block
-  static constexpr int SPB = KS + NVS;                   // slots per packed block
+  static constexpr int VPW = TPW / VT;                   // value slots per column
   static constexpr int VROWB = D * BITS / 8;             // bytes of one token's value codes
   static constexpr int VBOX = VROWB < 128 ? VROWB : 128; // TMA box width (bytes)
   static constexpr int NVB = VROWB / VBOX;               // boxes per value slot
@@ -125,19 +126,22 @@ struct Cfg {
   static constexpr int RVP = CPL == 8 ? 2 * D + 32 : 2 * D + 16;   // 8 / 4 words mod 32
   static constexpr int RSLOT_K = 16 * RKP;
   static constexpr int RSLOT_V = 8 * RVP;
-  static constexpr int RAW = KSLOT > VSLOT ? KSLOT : VSLOT;
-  static constexpr int RAWR = RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V;
+  static constexpr int PRAW = VSLOT > RSLOT_K ? (VSLOT > RSLOT_V ? VSLOT : RSLOT_V)
+                                              : (RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V);
   // Slots start on 1024-byte boundaries (required by the 128-byte swizzle).
-  static constexpr int SLOT = ((RAW > RAWR ? RAW : RAWR) + 1023) / 1024 * 1024;
+  static constexpr int VRSLOT = (PRAW + 1023) / 1024 * 1024;        // private slot
+  static constexpr int KSLOT_AL = (KSLOT + 1023) / 1024 * 1024;
   static constexpr int PBUF = 8 * NT * PPITCH;
-  static constexpr int WARP_BYTES = (RING * SLOT + KMETA + PBUF + 1023) / 1024 * 1024;
+  static constexpr int GROUP_BYTES = (RK * KSLOT_AL + 2 * KMETA + 1023) / 1024 * 1024;
+  static constexpr int WARP_BYTES = (RV * VRSLOT + PBUF + 1023) / 1024 * 1024;
   static constexpr int QFRAG = KSTEPS * NT * 32 * 8;
   static constexpr int QFRAG_AL = (QFRAG + 1023) / 1024 * 1024;
-  static constexpr int SMEM = 1024 + QFRAG_AL + WARPS * WARP_BYTES;  // + alignment slack
-  static constexpr int MERGE = WARPS * 8 * NT * (D + 2) * 4;
-  static_assert(MERGE <= WARPS * WARP_BYTES, "merge scratch must fit the warp region");
-  static_assert(2 * 16 * kMaxCph * 4 + 16 * 2 * 4 <= WARPS * WARP_BYTES,
-                "final-merge scratch (rows x CTAs per pair) must fit the warp region");
+  static constexpr int BODY = NGRP * GROUP_BYTES + NCW * WARP_BYTES;
+  static constexpr int SMEM = 1024 + QFRAG_AL + BODY;  // + alignment slack
+  static constexpr int MERGE = NCW * 8 * NT * (D + 2) * 4;
+  static_assert(MERGE <= BODY, "merge scratch must fit the group and warp regions");
+  static_assert(2 * 16 * kMaxCph * 4 + 16 * 2 * 4 <= BODY,
+                "final-merge scratch (rows x CTAs per pair) must fit");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
@@ -186,11 +190,11 @@ struct Warp {
   // Per-lane state.
   float acc[C::MTV][NT][4];
   float m[NT][2], l[NT][2];
-  float S[8][NT][4];          // 128 tokens: m-tile mt, rows r / r+8 <-> tokens 16r+2mt (+1)
+  float S[C::MTW][NT][4];     // column tokens: m-tile mt, rows r / r+8 <-> TPL*r+2mt (+1)
 
   int lane, r, qd;
   uint32_t qf;                // query fragments (shared address)
-  uint32_t ring, kmeta, pbuf; // per-warp shared regions
+  uint32_t ring, pbuf;        // private slot ring and P buffer
   float scale_log2;
 
   __device__ void init(int lane_, uint32_t qf_, uint32_t base, float sl) {
@@ -199,8 +203,7 @@ struct Warp {
     qd = lane & 3;
     qf = qf_;
     ring = base;
-    kmeta = base + RING * C::SLOT;
-    pbuf = kmeta + C::KMETA;
+    pbuf = base + RV * C::VRSLOT;
     scale_log2 = sl;
 #pragma unroll
     for (int i = 0; i < C::MTV; ++i)
@@ -219,7 +222,7 @@ struct Warp {
 
   __device__ __forceinline__ void zero_s() {
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt)
+    for (int mt = 0; mt < C::MTW; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -230,16 +233,6 @@ struct Warp {
   // Packed slot loads: lane 0 issues TMA tile copies (+ 1-D bulk copies of
   // the metadata) that complete on the slot's mbarrier.
   // ---------------------------------------------------------------------
-  __device__ void load_packed_k(const SeqDev &sd, int head, int unit, int ks, uint32_t slot,
-                                uint32_t bar) {
-    if (lane == 0) {
-      const bool meta = ks == 0;
-      mbar_expect_tx(bar, C::KSLOT + (meta ? C::KMETA : 0));
-      tma_load_4d(slot, &sd.tk, bar, 0, ks * C::KCH, unit, head);
-      if (meta) bulk_load(kmeta, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, bar);
-    }
-  }
-
   __device__ void load_packed_v(const SeqDev &sd, int head, int tok0, uint32_t slot, uint32_t bar) {
     if (lane == 0) {
       mbar_expect_tx(bar, C::VSLOT);
@@ -265,27 +258,20 @@ struct Warp {
   }
 
   // ---------------------------------------------------------------------
-  // QK^T over packed key slot ks (KCH channels x 128 tokens) into S.
+  // QK^T of this warp's column (tokens wi*TPW ..) over shared key slot ks.
   // ---------------------------------------------------------------------
-  __device__ void qk_packed(uint32_t slot, int ks) {
+  __device__ void qk_packed(uint32_t slot, int ks, int wi, uint32_t kmeta) {
     constexpr int STEPS = C::KCH / 16;
 #pragma unroll 1
     for (int sl = 0; sl < STEPS; ++sl) {
       const int s = ks * STEPS + sl;   // k-step (16 channels)
       // lane's channels: 2qd, 2qd+1, 2qd+8, 2qd+9 of the k-step
       float2 sc[4], lo[4];
-      uint32_t w[4][C::S / 32];   // 16 (Q8) or 8 (Q4) bytes of the lane's tokens
+      uint32_t w[4];              // 4 (Q8) or 8 (Q4) tokens of one channel
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int cl = 16 * sl + 2 * qd + (e & 1) + 8 * (e >> 1);   // row in the slot
-        const uint32_t addr = slot + swz<C::KSWZ>(cl * C::S + r * (C::S / 8));
-        if constexpr (C::S == 128) {
-          const uint4 v = lds128(addr);
-          w[e][0] = v.x; w[e][1] = v.y; w[e][2] = v.z; w[e][3] = v.w;
-        } else {
-          const uint2 v = lds64(addr);
-          w[e][0] = v.x; w[e][1] = v.y;
-        }
+        w[e] = lds32(slot + swz<C::KSWZ>(cl * C::S + wi * (C::S / C::GW) + 4 * r));
         const float2 sm = lds64f(kmeta + (16 * s + 2 * qd + (e & 1) + 8 * (e >> 1)) * 8);
         sc[e] = make_float2(sm.x, sm.x);
         lo[e] = make_float2(sm.y, sm.y);
@@ -294,20 +280,18 @@ struct Warp {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(qf + ((s * NT + nt) * 32 + lane) * 8);
 #pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        // m-tile mt: row r <-> token 16r+2mt, row r+8 <-> token 16r+2mt+1
+      for (int mt = 0; mt < C::MTW; ++mt) {
+        // m-tile mt: row r <-> token TPL*r+2mt, row r+8 <-> token TPL*r+2mt+1
         float2 x[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           if constexpr (BITS == 8) {
-            const uint32_t word = w[e][mt >> 1];
-            x[e] = (mt & 1) ? make_float2(byte_magic<2>(word), byte_magic<3>(word))
-                            : make_float2(byte_magic<0>(word), byte_magic<1>(word));
+            x[e] = mt ? make_float2(byte_magic<2>(w[e]), byte_magic<3>(w[e]))
+                      : make_float2(byte_magic<0>(w[e]), byte_magic<1>(w[e]));
           } else {
             // byte mt holds token 2mt (low nibble) and 2mt+1 (high nibble)
-            const uint32_t word = w[e][mt >> 2];
-            const uint32_t lo4 = word & 0x0F0F0F0Fu, hi4 = (word >> 4) & 0x0F0F0F0Fu;
-            const uint32_t sel = 0x7440u | (mt & 3);
+            const uint32_t lo4 = w[e] & 0x0F0F0F0Fu, hi4 = (w[e] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t sel = 0x7440u | mt;
             x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
                                __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
           }
