@@ -27,8 +27,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   using T = typename Elem<DT>::T;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int s_seq, s_last;
-  __shared__ __align__(8) uint64_t s_full[C::NGRP][RKMAX], s_empty[C::NGRP][RKMAX];
-  __shared__ __align__(8) uint64_t s_vfull[NCW][RV];
+  __shared__ __align__(8) uint64_t s_bar[WARPS][2];
   // 1024-byte aligned base: the 128-byte TMA swizzle needs aligned slots.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
@@ -49,229 +48,160 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const int head = local / sd.cph, split = local % sd.cph;
   const int G = p.group, rows = p.rows, nq = p.nq;
 
-  // ---- shared memory map ----------------------------------------------------
-  const uint32_t qf = smem_u32(smem);
-  const uint32_t groups = qf + C::QFRAG_AL;
-  const uint32_t warps = groups + C::NGRP * C::GROUP_BYTES;
-  auto kslot = [&](int g, int k) { return groups + g * C::GROUP_BYTES + k * C::KSLOT_AL; };
-  auto kmeta_of = [&](int g, int parity) {
-    return groups + g * C::GROUP_BYTES + C::RK * C::KSLOT_AL + parity * C::KMETA;
-  };
-  auto full_bar = [&](int g, int k) { return smem_u32(&s_full[g][k]); };
-  auto empty_bar = [&](int g, int k) { return smem_u32(&s_empty[g][k]); };
+  // ---- query fragments for both channel orders -----------------------------
+  const uint32_t qfp = smem_u32(smem), qfr = qfp + C::QFRAG;
+  const uint32_t bar0 = smem_u32(&s_bar[warp][0]), bar1 = smem_u32(&s_bar[warp][1]);
+  if (lane == 0) {
+    mbar_init(bar0, 1);
+    mbar_init(bar1, 1);
+    mbar_fence_init();
+  }
+  {
+    const uint16_t *q = static_cast<const uint16_t *>(sd.q);
+    for (int x = tid; x < C::KSTEPS * NT * 32; x += THREADS) {
+      const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
+      const int rr = ln >> 2, qq = ln & 3, row = 8 * nt + rr;
+      uint2 vp = make_uint2(0, 0), vr = make_uint2(0, 0);
+      if (row < rows) {
+        const int n = row / G, g = row % G;
+        const uint16_t *qrow = q + (head * G + g) * sd.q_h + n * sd.q_n;
+        const int cp = 16 * s + qq, cr = 16 * s + 4 * qq;
+        vp.x = qrow[cp] | (uint32_t(qrow[cp + 4]) << 16);
+        vp.y = qrow[cp + 8] | (uint32_t(qrow[cp + 12]) << 16);
+        vr.x = qrow[cr] | (uint32_t(qrow[cr + 1]) << 16);
+        vr.y = qrow[cr + 2] | (uint32_t(qrow[cr + 3]) << 16);
+      }
+      *reinterpret_cast<uint2 *>(smem + x * 8) = vp;
+      *reinterpret_cast<uint2 *>(smem + C::QFRAG + x * 8) = vr;
+    }
+  }
+  __syncthreads();
 
-  // ---- work items of this CTA --------------------------------------------------
-  // Packed blocks [ib, pe) go to groups round-robin; residual items [rs, ie)
-  // go to consumer warps round-robin.
+  // ---- this warp's work items ---------------------------------------------
   const int np = sd.ue - sd.ub;
   const int nr = (sd.re - sd.rb + 15) / 16;
   const int ni = np + nr;
   const int ib = int(int64_t(split) * ni / sd.cph);
   const int ie = int(int64_t(split + 1) * ni / sd.cph);
-  const int pe = ie < np ? ie : np;
-  const int nbc = pe > ib ? pe - ib : 0;                  // packed blocks in this CTA
-  const int rs = ib > np ? ib : np;
-  const int nrc = ie > rs ? ie - rs : 0;                  // residual items in this CTA
-  auto group_blocks = [&](int g) { return nbc > g ? (nbc - g + C::NGRP - 1) / C::NGRP : 0; };
-  bool failed = false;
+  const int first = ib + warp;
+  const int kt = ie > first ? (ie - first + WARPS - 1) / WARPS : 0;
+  const int pend = ie < np ? ie : np;
+  const int kp = pend > first ? (pend - first + WARPS - 1) / WARPS : 0;
+  const int total = kp * C::SPB + (kt - kp) * 2;
 
-  {
-    // ======================= consumer warps ===================================
-    const int g = warp / C::GW, wi = warp % C::GW;
-    const int nb = group_blocks(g);
-    const int nrw = nrc > warp ? (nrc - warp + NCW - 1) / NCW : 0;
-    const int nv = nb * C::VPW + nrw * 4;                // private slots
-    const uint32_t vbar0 = smem_u32(&s_vfull[warp][0]);
-    Warp<BITS, D, NT, DT> w;
-    w.init(lane, qf, warps + warp * C::WARP_BYTES, p.scale_log2);
-    const T *rk = static_cast<const T *>(sd.rk) + head * sd.rk_h;
-    const T *rv = static_cast<const T *>(sd.rv) + head * sd.rv_h;
-    const int length = sd.length, packed = sd.packed;
-    const int rr = lane >> 2;
+  Warp<BITS, D, NT, DT> w;
+  w.init(lane, qfp, qfr, qfp + C::QFRAG_AL + warp * C::WARP_BYTES, p.scale_log2);
 
-    auto vslot = [&](int v) { return w.ring + (v % RV) * C::VRSLOT; };
-    auto vbar = [&](int v) { return vbar0 + 8 * (v % RV); };
-    auto is_tma = [&](int v) { return v < nb * C::VPW; };
-    auto resid_t0 = [&](int v) {
-      const int k = (v - nb * C::VPW) >> 2;
-      return sd.rb + (rs - np + warp + k * NCW) * 16;
-    };
-    auto issue_v = [&](int v) {
-      if (is_tma(v)) {
-        const int jb = v / C::VPW, j = v % C::VPW;
-        const int unit = sd.ub + ib + g + jb * C::NGRP;
-        w.load_packed_v(sd, head, unit * 128 + wi * C::TPW + j * C::VT, vslot(v), vbar(v));
+  const T *rk = static_cast<const T *>(sd.rk) + head * sd.rk_h;
+  const T *rv = static_cast<const T *>(sd.rv) + head * sd.rv_h;
+  const int length = sd.length, packed = sd.packed;
+
+  auto is_tma = [&](int s) { return s < kp * C::SPB; };
+  auto issue = [&](int s) {
+    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
+    const uint32_t bar = (s & 1) ? bar1 : bar0;
+    if (is_tma(s)) {
+      const int k = s / C::SPB, part = s % C::SPB;
+      const int unit = sd.ub + first + k * WARPS;
+      const int qq = part / (1 + C::VSQ), sub = part % (1 + C::VSQ);
+      if (sub == 0)
+        w.load_packed_k(sd, head, unit, qq, slot, qq == 0, bar);
+      else
+        w.load_packed_v(sd, head, unit * 128 + qq * C::QT + (sub - 1) * 32, slot, bar);
+    } else {
+      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
+      const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
+      if (part == 0)
+        w.load_resid(rk, sd.rk_t, t0, sd.re, slot, C::RKP);
+      else
+        w.load_resid(rv, sd.rv_t, t0, sd.re, slot, C::RVP);
+    }
+  };
+
+  const int rr = lane >> 2;
+  auto compute = [&](int s) {
+    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
+    if (is_tma(s)) {
+      const int part = s % C::SPB;
+      const int sub = part % (1 + C::VSQ);
+      if (sub == 0) {
+        w.qk_packed(slot);
+        w.template softmax<C::MTQ>(
+            [&](int mt, int h) { return C::TPL * rr + 2 * mt + h; },
+            [](int, int) { return true; }, [](int t) { return packed_pos(t); });
       } else {
-        const int part = (v - nb * C::VPW) & 3, t0 = resid_t0(v);
-        if (part < 2)
-          w.load_resid(rk, sd.rk_t, t0, sd.re, 16, part * (D / 2), D / 2, vslot(v), C::RKP);
-        else
-          w.load_resid(rv, sd.rv_t, t0 + 8 * (part - 2), sd.re, 8, 0, D, vslot(v), C::RVP);
+        w.pv_packed(slot, 2 * (sub - 1));
       }
-    };
-    // Private ring: every issue commits one cp.async group (empty for TMA
-    // slots), so residual slots wait with cp.async.wait_group RV-2.
-    uint32_t vphase = 0;
-    auto wait_v = [&](int v) -> bool {
-      if (is_tma(v)) {
-        const int k = v % RV;
-        if (!mbar_wait(vbar(v), (vphase >> k) & 1)) return false;
-        vphase ^= 1u << k;
+    } else {
+      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
+      if (part == 0) {
+        const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
+        w.qk_resid(slot);
+        w.template softmax<1>(
+            [&](int, int h) { return rr + 8 * h; },
+            [&](int t, int row) {
+              const int ri = t0 + t;
+              return ri < sd.re && (nq == 1 || packed + ri <= length - nq + row / G);
+            },
+            [](int t) { return resid_pos<C::CPL>(t); });
       } else {
-        cp_async_wait<RV - 2>();
+        w.pv_resid(slot);
       }
-      __syncwarp();
-      return true;
-    };
-    int v_next = 0;   // next private slot to consume
-    auto release_v = [&]() {
-      __syncwarp();
-      if (v_next + RV - 1 < nv) issue_v(v_next + RV - 1);
-      cp_async_commit();
-      ++v_next;
-    };
+    }
+  };
 
-    // Shared key slots of the group, issued by its first warp (lane 0).
-    const bool leader = wi == 0;
-    const int nk = nb * C::KS;
-    auto issue_k = [&](int i) -> bool {
-      const int k = i % C::RK;
-      if (i >= C::RK && !mbar_wait(empty_bar(g, k), ((i / C::RK) - 1) & 1)) return false;
-      const int jb = i / C::KS, ks = i % C::KS;
-      const int unit = sd.ub + ib + g + jb * C::NGRP;
-      const bool meta = ks == 0;
-      const uint32_t bar = full_bar(g, k);
-      mbar_expect_tx(bar, C::KSLOT + (meta ? C::KMETA : 0));
-      tma_load_4d(kslot(g, k), &sd.tk, bar, 0, ks * C::KCH, unit, head);
-      if (meta)
-        bulk_load(kmeta_of(g, jb & 1), sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA,
-                  bar);
-      return true;
-    };
-    if (lane == 0) {
-      for (int k = 0; k < RV; ++k) mbar_init(vbar0 + 8 * k, 1);
-      if (leader) {
-        for (int k = 0; k < C::RK; ++k) {
-          mbar_init(full_bar(g, k), 1);
-          mbar_init(empty_bar(g, k), C::GW);
-        }
+  // Every slot commits one cp.async group (empty for TMA slots), so the
+  // residual slots can wait with cp.async.wait_group 1; TMA slots wait on
+  // their mbarrier phase.
+  uint32_t phase = 0;  // bit k: parity of the next completion of ring slot k
+  __syncwarp();
+  if (total > 0) issue(0);
+  cp_async_commit();
+  if (total > 1) issue(1);
+  cp_async_commit();
+  int s = 0;
+  for (; s < total; ++s) {
+    if (is_tma(s)) {
+      const int k = s & 1;
+      if (!mbar_wait(k ? bar1 : bar0, (phase >> k) & 1)) {
+        if (lane == 0) atomicOr(p.error, 1u);
+        break;
       }
-      mbar_fence_init();
-      if (leader)
-        for (int i = 0; i < C::RK - 1 && i < nk; ++i) issue_k(i);
+      phase ^= 1u << k;
+    } else {
+      cp_async_wait<1>();
     }
     __syncwarp();
-    for (int k = 0; k < RV - 1; ++k) {
-      if (k < nv) issue_v(k);
-      cp_async_commit();
-    }
-    // Query fragments (MMA B operand, k-index 2qd+b <-> channel 2qd+b), built
-    // by the consumer warps while the first slots are in flight.
-    {
-      const uint16_t *q = static_cast<const uint16_t *>(sd.q);
-      for (int x = tid; x < C::KSTEPS * NT * 32; x += NCW * 32) {
-        const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
-        const int r2 = ln >> 2, qq = ln & 3, row = 8 * nt + r2;
-        uint2 val = make_uint2(0, 0);
-        if (row < rows) {
-          const int n = row / G, gg = row % G;
-          const uint16_t *qrow = q + (head * G + gg) * sd.q_h + n * sd.q_n;
-          const int c = 16 * s + 2 * qq;
-          val.x = qrow[c] | (uint32_t(qrow[c + 1]) << 16);
-          val.y = qrow[c + 8] | (uint32_t(qrow[c + 9]) << 16);
-        }
-        *reinterpret_cast<uint2 *>(smem + x * 8) = val;
-      }
-    }
-    named_sync(1, THREADS);   // barriers initialised
-    named_sync(1, THREADS);   // query fragments published
+    compute(s);
+    __syncwarp();
+    if (s + 2 < total) issue(s + 2);
+    cp_async_commit();
+  }
+  if (s < total) {
+    // A wait gave up: let the copies still in flight land (bounded) before
+    // this CTA's shared memory is reused or released.
+    for (int k2 = s; k2 < s + 2 && k2 < total; ++k2)
+      if (is_tma(k2)) mbar_wait((k2 & 1) ? bar1 : bar0, (phase >> (k2 & 1)) & 1);
+  }
+  cp_async_wait<0>();
 
-    // ---- packed blocks of the group: this warp's token column ---------------
-    for (int jb = 0; jb < nb && !failed; ++jb) {
-      for (int ks = 0; ks < C::KS; ++ks) {
-        const int i = jb * C::KS + ks, k = i % C::RK;
-        if (!mbar_wait(full_bar(g, k), (i / C::RK) & 1)) {
-          failed = true;
-          break;
-        }
-        if (ks == 0) w.zero_s();
-        w.qk_packed(kslot(g, k), ks, wi, kmeta_of(g, jb & 1));
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(empty_bar(g, k));
-          // Refill: slot i + RK - 1 reuses the ring position of slot i - 1.
-          if (leader && i + C::RK - 1 < nk && !issue_k(i + C::RK - 1)) failed = true;
-        }
-        failed = __shfl_sync(0xffffffffu, failed, 0);
-        if (failed) break;
-      }
-      if (failed) break;
-      w.template softmax<C::MTW>([&](int mt, int h) { return C::TPL * rr + 2 * mt + h; },
-                                 [](int, int) { return true; },
-                                 [](int t) { return packed_pos(t); });
-      for (int j = 0; j < C::VPW; ++j) {
-        if (!wait_v(v_next)) {
-          failed = true;
-          break;
-        }
-        w.pv_packed(vslot(v_next), j);
-        release_v();
-      }
-    }
-    // ---- residual items of this warp ---------------------------------------
-    for (int k = 0; k < nrw && !failed; ++k) {
-      for (int part = 0; part < 4; ++part) {
-        if (!wait_v(v_next)) {
-          failed = true;
-          break;
-        }
-        const uint32_t slot = vslot(v_next);
-        if (part < 2) {
-          if (part == 0) w.zero_s();
-          w.qk_resid(slot, part);
-          if (part == 1) {
-            const int t0 = resid_t0(v_next);
-            w.template softmax<1>(
-                [&](int, int h) { return rr + 8 * h; },
-                [&](int t, int row) {
-                  const int ri = t0 + t;
-                  return ri < sd.re && (nq == 1 || packed + ri <= length - nq + row / G);
-                },
-                [](int t) { return resid_pos<C::CPL>(t); });
-          }
-        } else {
-          w.pv_resid(slot, part - 2);
-        }
-        release_v();
-      }
-    }
-    if (failed) {
-      if (lane == 0) atomicOr(p.error, 1u);
-      // Let this warp's copies still in flight land (bounded) before exit.
-      for (int v = v_next; v < v_next + RV - 1 && v < nv; ++v)
-        if (is_tma(v)) mbar_wait(vbar(v), (vphase >> (v % RV)) & 1);
-    }
-    if (leader && lane == 0) {
-      // The group's last key copies must land before the CTA can finish.
-      for (int j = nk > C::RK ? nk - C::RK : 0; j < nk; ++j)
-        mbar_wait(full_bar(g, j % C::RK), (j / C::RK) & 1);
-    }
-    cp_async_wait<0>();
-
-    // ---- this warp's state -> merge scratch ----------------------------------
+  // ---- warp -> CTA merge ----------------------------------------------------
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float v = w.l[nt][j];
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        v += __shfl_xor_sync(0xffffffffu, v, 8);
-        v += __shfl_xor_sync(0xffffffffu, v, 16);
-        w.l[nt][j] = v;
-      }
-    named_sync(2, THREADS);   // every warp is done with the slot rings
-    float *mw = reinterpret_cast<float *>(smem + C::QFRAG_AL) + warp * 8 * NT * D;
-    float *mlw = reinterpret_cast<float *>(smem + C::QFRAG_AL) + NCW * 8 * NT * D;
+    for (int j = 0; j < 2; ++j) {
+      float v = w.l[nt][j];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      w.l[nt][j] = v;
+    }
+  __syncthreads();  // ring memory becomes merge scratch
+  constexpr int WR = 8 * NT;  // rows held by a warp
+  float *mrg = reinterpret_cast<float *>(smem + C::QFRAG_AL);
+  float *ml = mrg + WARPS * WR * D;
+  {
+    float *mw = mrg + warp * WR * D;
 #pragma unroll
     for (int i = 0; i < C::MTV; ++i)
 #pragma unroll
@@ -287,16 +217,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int row = 8 * nt + 2 * w.qd + j;
-          mlw[(warp * 8 * NT + row) * 2] = w.m[nt][j];
-          mlw[(warp * 8 * NT + row) * 2 + 1] = w.l[nt][j];
+          ml[(warp * WR + row) * 2] = w.m[nt][j];
+          ml[(warp * WR + row) * 2 + 1] = w.l[nt][j];
         }
     }
   }
-
-  // ---- warp -> CTA merge ----------------------------------------------------
-  constexpr int WR = 8 * NT;  // rows held by a warp
-  float *mrg = reinterpret_cast<float *>(smem + C::QFRAG_AL);
-  float *ml = mrg + NCW * WR * D;
   __syncthreads();
   float *rec = p.rec + size_t(cta) * rows * D;
   float *recml = p.rec_ml + size_t(cta) * rows * 2;
@@ -347,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     s_l[row * cph + c] = ml2.y;
   }
   __syncthreads();
-  for (int row = warp; row < rows; row += THREADS / 32) {
+  for (int row = warp; row < rows; row += WARPS) {
     float M = -INFINITY;
     for (int c = lane; c < cph; c += 32) M = fmaxf(M, s_w[row * cph + c]);
 #pragma unroll
@@ -566,14 +491,13 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
     set_last_error("cuTensorMapEncodeTiled unavailable");
     return CKV_ERR_CUDA;
   }
-  constexpr uint64_t S = C::S;
+  constexpr uint64_t S = 128 * BITS / 8;
   const cuuint64_t kdims[4] = {S, cuuint64_t(D), cuuint64_t(s.unit_end), cuuint64_t(hkv)};
   const cuuint64_t kstr[3] = {S, cuuint64_t(s.kd_stride_unit), cuuint64_t(s.kd_stride_head)};
-  const cuuint32_t kbox[4] = {cuuint32_t(S), cuuint32_t(C::KCH), 1, 1};
+  const cuuint32_t kbox[4] = {32, cuuint32_t(D), 1, 1};
   const cuuint32_t one[4] = {1, 1, 1, 1};
   CUresult r = enc(&d.tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(s.key_data), kdims,
-                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   S == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("key tensor map rejected (bank strides)");
@@ -581,7 +505,7 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   }
   const cuuint64_t vdims[3] = {cuuint64_t(C::VROWB), cuuint64_t(s.unit_end) * 128, cuuint64_t(hkv)};
   const cuuint64_t vstr[2] = {cuuint64_t(s.vd_stride_token), cuuint64_t(s.vd_stride_head)};
-  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), cuuint32_t(C::VT), 1};
+  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), 32, 1};
   const CUtensorMapSwizzle swz = C::VBOX == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : C::VBOX == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                  : CU_TENSOR_MAP_SWIZZLE_32B;

@@ -1,22 +1,19 @@
 // Split-KV GQA attention over the compressed KV cache (sm_100a).
 //
 // One launch covers every (sequence, KV head) pair of a call.  Each pair is
-// split across `cph` CTAs.  A CTA holds NCW warps in groups of GW:
-//   * packed blocks (128 tokens) go to groups; the GW warps of a group split
-//     a block's tokens into columns of TPW = 128/GW tokens.  Key slots (KCH
-//     channels x 128 tokens, one TMA box of 128-token rows) are shared by the
-//     group: the group's first warp streams them through the group's RK-slot
-//     ring (full/empty mbarriers), RK-1 slots ahead of its own consumption.
-//     Each warp streams its own value slots (16 tokens x all channels) and
-//     residual slots through a private RV-slot ring;
-//   * residual items (16 exact tokens) go to single consumer warps;
-//   * every consumer warp keeps its own online-softmax state; warps merge
-//     inside the CTA, CTAs merge in the last CTA of the pair (atomic ticket),
-//     all in one launch.
-// Packed tiles arrive by TMA (cp.async.bulk.tensor from per-sequence tensor
-// maps, metadata by 1-D bulk copies); the exact residual by 16-byte
-// cp.async.  Every wait on a barrier is bounded (about a second) and flags an
-// error instead of hanging.
+// split across `cph` CTAs; each CTA splits its share across WARPS warps; each
+// warp streams its own work items through a private two-slot ring in shared
+// memory and keeps its own online-softmax state.  Packed tiles arrive by TMA
+// (cp.async.bulk.tensor from per-sequence tensor maps, metadata by 1-D bulk
+// copies) signalled on one mbarrier per slot; the exact residual arrives by
+// 16-byte cp.async.  Warps merge inside the CTA, CTAs merge in the last CTA of
+// the pair (atomic ticket), all in one launch.
+//
+// Work items:
+//   packed block  -- 128 tokens of one KV head, consumed in "quarters" of
+//                    32 (Q8) or 64 (Q4) tokens: a K slot (all channels of the
+//                    quarter's tokens) then one or two V slots of 32 tokens.
+//   residual item -- 16 exact bf16/fp16 tokens of the recent window.
 //
 // Numerics follow models/compressed_kv_kernels.py:_partial (:12-77): a code
 // is dequantized as fma(code, scale, low) and rounded to the query dtype
@@ -29,15 +26,16 @@
 // tokens or channels on M and the query rows (n, g) on N.  QK^T is
 // S^T[token][row] = K^T[token][channel] q^T[channel][row]; PV is
 // O^T[channel][row] = V^T[channel][token] P^T[token][row].  Codes are
-// dequantized straight into A fragments in registers.  MMA k-index 2qd+b
-// (+8) maps to channel / token 2qd+b (+8) of the k-step; the reduction order
-// is free, so rows (M) are permuted instead:
-//   * key slot rows are channels of 128 (Q8) or 64 (Q4) bytes, loaded with
-//     the TMA 128/64-byte swizzle (16-byte chunk c of row y lands at c ^ f(y));
-//     in its column, lane r owns tokens TPL*r .. TPL*r+TPL-1 (one 4-byte
-//     load per channel); for Q8 the 32 lanes hit 32 different banks;
-//   * value slot rows are tokens, loaded as 128-byte swizzled boxes; lane r
-//     owns CPL channels per chunk;
+// dequantized straight into A fragments in registers.  Because the reduction
+// order inside an MMA is free, channels and tokens are permuted so that every
+// shared-memory read is conflict-free without a swizzle:
+//   * K slot rows are channels (32 bytes each); A-fragment k-index 2qd+e
+//     maps to channel 16s+qd+4e', so the four lanes of a row group read rows
+//     8 words apart.
+//   * V slot rows are tokens, loaded as 128-byte boxes with the TMA 128-byte
+//     swizzle (16-byte chunk c of row t lands at chunk c ^ (t & 7)); with the
+//     natural PV token order (k-index 2qd+b <-> token 2qd+b) the 8 lanes of a
+//     quarter-warp read 8 different chunks.
 //   * P is stored permuted so each lane's B fragment is one 8-byte load.
 #pragma once
 
@@ -48,16 +46,13 @@
 namespace ckv {
 namespace attn {
 
-constexpr int NCW = 8;               // consumer warps per CTA (one CTA per SM)
-constexpr int WARPS = NCW;           // warps holding softmax state
-constexpr int THREADS = NCW * 32;
-constexpr int RKMAX = 4;             // key slots per group ring (at most)
-constexpr int RV = 3;                // value / residual slots per consumer ring
-constexpr int PPITCH = 160;          // bytes per P row (<= 64 tokens + pad), 40 words
+constexpr int WARPS = 8;
+constexpr int THREADS = WARPS * 32;
+constexpr int PPITCH = 160;          // bytes per P row (<= 64 tokens), 40 words
 
 struct alignas(64) SeqDev {
-  CUtensorMap tk;   // key codes   [H][units][D][S] bytes; box S bytes x KC channels
-  CUtensorMap tv;   // value codes [H][tokens][D*bits/8] bytes; box VBOX bytes x 16 tokens
+  CUtensorMap tk;   // key codes   [H][units][D][S] bytes, box 32 bytes x D channels
+  CUtensorMap tv;   // value codes [H][tokens][D*bits/8] bytes, box VBOX bytes x 32 tokens
   const void *q;
   const float *km;
   const float *vm;
@@ -82,7 +77,7 @@ struct ParamsHead {
   unsigned *error;      // set to 1 when a wait gives up
 };
 
-// Kernel parameters: a single-sequence call passes a ~400-byte block, a
+// Kernel parameters: a single-sequence call passes a ~300-byte block, a
 // batched call the full table (launch cost grows with parameter size).
 template <int MAXS>
 struct alignas(64) Params : ParamsHead {
@@ -94,55 +89,44 @@ constexpr int kMaxCph = 256;  // CTAs per (sequence, KV head), bounded by the me
 template <int BITS, int D, int NT>
 struct Cfg {
   static constexpr int KSTEPS = D / 16;
-  static constexpr int S = 128 * BITS / 8;              // key bytes per channel row (128 tokens)
-  static constexpr int KC = BITS == 8 ? 32 : 64;         // channels per key slot
-  static constexpr int KCH = D < KC ? D : KC;            // channels actually in a key slot
-  static constexpr int KS = D / KCH;                     // key slots per block
-  static constexpr int KSLOT = KCH * S;                  // key slot bytes
-  static constexpr int KSWZ = S == 128 ? 7 : 3;          // key swizzle row mask (128 / 64 B)
-  static constexpr int KMETA = D * 8;                    // key (scale, low) of one block
-  static constexpr int GW = BITS == 8 ? 4 : 2;           // consumer warps per group
-  static constexpr int RK = GW == 4 ? RKMAX : 3;         // key slots per group ring
-  static constexpr int NGRP = NCW / GW;                  // groups per CTA
-  static constexpr int TPW = 128 / GW;                   // tokens per warp column
-  static constexpr int TPL = TPW / 8;                    // tokens per lane (4 B of codes)
-  static constexpr int MTW = TPW / 16;                   // m-tiles per column
-  static constexpr int VT = 16;                          // tokens per value slot
-  static constexpr int VPW = TPW / VT;                   // value slots per column
-  static constexpr int VROWB = D * BITS / 8;             // bytes of one token's value codes
+  static constexpr int QT = BITS == 8 ? 32 : 64;        // tokens per K slot
+  static constexpr int QPB = 128 / QT;                  // K slots per block
+  static constexpr int TPL = QT / 8;                    // tokens per lane in a K slot
+  static constexpr int MTQ = QT / 16;                   // m-tiles per K slot
+  static constexpr int VSQ = QT / 32;                   // V slots per K slot
+  static constexpr int SPB = QPB * (1 + VSQ);           // slots per packed block
+  static constexpr int KSLOT = D * 32;                  // K slot bytes (TMA box 32 B x D)
+  static constexpr int KMETA = D * 8;                   // key (scale, low) of one block
+  static constexpr int VROWB = D * BITS / 8;            // bytes of one token's value codes
   static constexpr int VBOX = VROWB < 128 ? VROWB : 128; // TMA box width (bytes)
-  static constexpr int NVB = VROWB / VBOX;               // boxes per value slot
-  static constexpr int VSWZ = VBOX == 128 ? 7 : (VBOX == 64 ? 3 : 1);
+  static constexpr int NVB = VROWB / VBOX;              // boxes per value slot
+  static constexpr int VSWZ = VBOX == 128 ? 7 : (VBOX == 64 ? 3 : 1);  // swizzle row mask
   static constexpr int NG = D / 64;
-  static constexpr int VMETA = VT * NG * 8;              // value (scale, low) of VT tokens
-  static constexpr int VSLOT = VT * VROWB + VMETA;
+  static constexpr int VMETA = 32 * NG * 8;             // value (scale, low) of 32 tokens
+  static constexpr int VSLOT = 32 * VROWB + VMETA;
   // Value lane mapping: lane r owns CPL channels in each of NCH chunks.
   static constexpr int CPL = BITS == 8 ? (D >= 128 ? 16 : 8) : D / 8;
   static constexpr int NCH = D / (8 * CPL);
-  static constexpr int MTC = CPL / 2;                    // output m-tiles per chunk
-  static constexpr int MTV = D / 16;                     // output m-tiles
-  // Residual slots: keys as 16 tokens x D/2 channels, values as 8 tokens x D.
-  static constexpr int RKP = D + 32 > 160 ? D + 32 : 160;          // 8 words mod 32
-  static constexpr int RVP = CPL == 8 ? 2 * D + 32 : 2 * D + 16;   // 8 / 4 words mod 32
+  static constexpr int MTC = CPL / 2;                   // m-tiles per chunk
+  static constexpr int MTV = D / 16;                    // m-tiles of the output
+  // Residual slots (16 tokens of 16-bit values, padded pitch, cp.async).
+  static constexpr int RKP = 2 * D + 32;
+  static constexpr int RVP = CPL == 8 ? 2 * D + 32 : 2 * D + 16;
   static constexpr int RSLOT_K = 16 * RKP;
-  static constexpr int RSLOT_V = 8 * RVP;
-  static constexpr int PRAW = VSLOT > RSLOT_K ? (VSLOT > RSLOT_V ? VSLOT : RSLOT_V)
-                                              : (RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V);
+  static constexpr int RSLOT_V = 16 * RVP;
+  static constexpr int SLOT_RAW = KSLOT > VSLOT ? KSLOT : VSLOT;
+  static constexpr int SLOT_R = RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V;
   // Slots start on 1024-byte boundaries (required by the 128-byte swizzle).
-  static constexpr int VRSLOT = (PRAW + 1023) / 1024 * 1024;        // private slot
-  static constexpr int KSLOT_AL = (KSLOT + 1023) / 1024 * 1024;
+  static constexpr int SLOT = ((SLOT_RAW > SLOT_R ? SLOT_RAW : SLOT_R) + 1023) / 1024 * 1024;
   static constexpr int PBUF = 8 * NT * PPITCH;
-  static constexpr int GROUP_BYTES = (RK * KSLOT_AL + 2 * KMETA + 1023) / 1024 * 1024;
-  static constexpr int WARP_BYTES = (RV * VRSLOT + PBUF + 1023) / 1024 * 1024;
-  static constexpr int QFRAG = KSTEPS * NT * 32 * 8;
-  static constexpr int QFRAG_AL = (QFRAG + 1023) / 1024 * 1024;
-  static constexpr int BODY = NGRP * GROUP_BYTES + NCW * WARP_BYTES;
-  static constexpr int SMEM = 1024 + QFRAG_AL + BODY;  // + alignment slack
-  static constexpr int MERGE = NCW * 8 * NT * (D + 2) * 4;
-  static_assert(MERGE <= BODY, "merge scratch must fit the group and warp regions");
-  static_assert(2 * 16 * kMaxCph * 4 + 16 * 2 * 4 <= BODY,
-                "final-merge scratch (rows x CTAs per pair) must fit");
-  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static constexpr int WARP_BYTES = (2 * SLOT + KMETA + PBUF + 1023) / 1024 * 1024;
+  static constexpr int QFRAG = KSTEPS * NT * 32 * 8;    // one fragment set
+  static constexpr int QFRAG_AL = (2 * QFRAG + 1023) / 1024 * 1024;
+  static constexpr int SMEM = 1024 + QFRAG_AL + WARPS * WARP_BYTES;  // + alignment slack
+  static constexpr int MERGE = WARPS * 8 * NT * (D + 2) * 4;
+  static_assert(MERGE <= WARPS * WARP_BYTES, "merge scratch must fit the warp region");
+  static_assert(2 * 16 * 256 * 4 + 16 * 2 * 4 <= WARPS * WARP_BYTES,
+                "final-merge scratch (rows x CTAs per pair) must fit the warp region");
 };
 
 // Offset of byte `a` of a TMA box (rows of 128/64/32 bytes) after the hardware
@@ -153,8 +137,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t a) {
   return a ^ (((a >> 7) & MASK) << 4);
 }
 
-// Residual P.V token order: k-index (qd, e) -> token A[qd] + B[e] of the
-// 16-token item (e = 0, 1 in the first 8 tokens, e = 2, 3 in the last 8).
+// Residual PV token order: k-index (qd, e) -> token A[qd] + B[e].
 template <int CPL>
 __device__ __forceinline__ int resid_token(int qd, int e) {
   if constexpr (CPL == 16) {
@@ -174,7 +157,7 @@ __device__ __forceinline__ int resid_pos(int t) {
     return 4 * (t & 3) + (t >> 2);
   }
 }
-// Position of packed token t (0..127) in the permuted P row: within each
+// Position of packed token t (0..63) in the permuted P row: within each
 // 16-token k-step, lane qd's four tokens 2qd, 2qd+1, 2qd+8, 2qd+9 sit at
 // 4qd..4qd+3 so its B fragment is one 8-byte load.
 __device__ __forceinline__ int packed_pos(int t) {
@@ -190,20 +173,22 @@ struct Warp {
   // Per-lane state.
   float acc[C::MTV][NT][4];
   float m[NT][2], l[NT][2];
-  float S[C::MTW][NT][4];     // column tokens: m-tile mt, rows r / r+8 <-> TPL*r+2mt (+1)
+  float S[C::MTQ][NT][4];
 
   int lane, r, qd;
-  uint32_t qf;                // query fragments (shared address)
-  uint32_t ring, pbuf;        // private slot ring and P buffer
+  uint32_t qfp, qfr;          // fragment sets (shared addresses)
+  uint32_t ring, kmeta, pbuf; // per-warp shared regions
   float scale_log2;
 
-  __device__ void init(int lane_, uint32_t qf_, uint32_t base, float sl) {
+  __device__ void init(int lane_, uint32_t qfp_, uint32_t qfr_, uint32_t base, float sl) {
     lane = lane_;
     r = lane >> 2;
     qd = lane & 3;
-    qf = qf_;
+    qfp = qfp_;
+    qfr = qfr_;
     ring = base;
-    pbuf = base + RV * C::VRSLOT;
+    kmeta = base + 2 * C::SLOT;
+    pbuf = kmeta + C::KMETA;
     scale_log2 = sl;
 #pragma unroll
     for (int i = 0; i < C::MTV; ++i)
@@ -220,109 +205,118 @@ struct Warp {
       }
   }
 
-  __device__ __forceinline__ void zero_s() {
-#pragma unroll
-    for (int mt = 0; mt < C::MTW; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) S[mt][nt][c] = 0.f;
-  }
-
   // ---------------------------------------------------------------------
   // Packed slot loads: lane 0 issues TMA tile copies (+ 1-D bulk copies of
   // the metadata) that complete on the slot's mbarrier.
   // ---------------------------------------------------------------------
+  __device__ void load_packed_k(const SeqDev &sd, int head, int unit, int quarter, uint32_t slot,
+                                bool with_meta, uint32_t bar) {
+    if (lane == 0) {
+      mbar_expect_tx(bar, C::KSLOT + (with_meta ? C::KMETA : 0));
+      tma_load_4d(slot, &sd.tk, bar, quarter * 32, 0, unit, head);
+      if (with_meta)
+        bulk_load(kmeta, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, bar);
+    }
+  }
+
   __device__ void load_packed_v(const SeqDev &sd, int head, int tok0, uint32_t slot, uint32_t bar) {
     if (lane == 0) {
       mbar_expect_tx(bar, C::VSLOT);
 #pragma unroll
       for (int bx = 0; bx < C::NVB; ++bx)
-        tma_load_3d(slot + bx * C::VT * C::VBOX, &sd.tv, bar, bx * C::VBOX, tok0, head);
-      bulk_load(slot + C::VT * C::VROWB, sd.vm + head * sd.vm_h + int64_t(tok0) * sd.vm_t, C::VMETA,
-                bar);
+        tma_load_3d(slot + bx * 32 * C::VBOX, &sd.tv, bar, bx * C::VBOX, tok0, head);
+      bulk_load(slot + 32 * C::VROWB, sd.vm + head * sd.vm_h + int64_t(tok0) * sd.vm_t, C::VMETA, bar);
     }
   }
 
-  // Residual rows [t0, t0 + rows) x channels [c0, c0 + nch) into a padded
-  // slot (rows at or past `re` are zero-filled).
-  __device__ void load_resid(const T *base, int64_t stride_t, int t0, int re, int rows, int c0,
-                             int nch, uint32_t slot, int pitch) {
-    const int chunks = nch / 8;  // 16-byte chunks per row
-    for (int x = lane; x < rows * chunks; x += 32) {
-      const int t = x / chunks, k = x % chunks;
+  // 16 residual tokens starting at window index t0 (rows >= re are zeroed).
+  __device__ void load_resid(const void *base_, int64_t stride_t, int t0, int re, uint32_t slot,
+                             int pitch) {
+    const T *base = static_cast<const T *>(base_);
+    constexpr int CH = D / 8;  // 16-byte chunks per row
+#pragma unroll 4
+    for (int x = lane; x < 16 * CH; x += 32) {
+      const int t = x / CH, k = x % CH;
       const bool ok = t0 + t < re;
-      const T *src = base + (ok ? int64_t(t0 + t) * stride_t : 0) + c0 + k * 8;
+      const T *src = base + (ok ? int64_t(t0 + t) * stride_t : 0) + k * 8;
       cp_async16(slot + t * pitch + k * 16, src, ok ? 16 : 0);
     }
   }
 
   // ---------------------------------------------------------------------
-  // QK^T of this warp's column (tokens wi*TPW ..) over shared key slot ks.
+  // QK^T over a packed K slot -> S (MTQ m-tiles of tokens x NT n-tiles)
   // ---------------------------------------------------------------------
-  __device__ void qk_packed(uint32_t slot, int ks, int wi, uint32_t kmeta) {
-    constexpr int STEPS = C::KCH / 16;
-#pragma unroll 1
-    for (int sl = 0; sl < STEPS; ++sl) {
-      const int s = ks * STEPS + sl;   // k-step (16 channels)
-      // lane's channels: 2qd, 2qd+1, 2qd+8, 2qd+9 of the k-step
-      float2 sc[4], lo[4];
-      uint32_t w[4];              // 4 (Q8) or 8 (Q4) tokens of one channel
+  __device__ void qk_packed(uint32_t slot) {
+#pragma unroll
+    for (int mt = 0; mt < C::MTQ; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) S[mt][nt][c] = 0.f;
+#pragma unroll 2
+    for (int s = 0; s < C::KSTEPS; ++s) {
+      float f[4][C::TPL];  // [channel e][token within lane]
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int cl = 16 * sl + 2 * qd + (e & 1) + 8 * (e >> 1);   // row in the slot
-        w[e] = lds32(slot + swz<C::KSWZ>(cl * C::S + wi * (C::S / C::GW) + 4 * r));
-        const float2 sm = lds64f(kmeta + (16 * s + 2 * qd + (e & 1) + 8 * (e >> 1)) * 8);
-        sc[e] = make_float2(sm.x, sm.x);
-        lo[e] = make_float2(sm.y, sm.y);
+        const int c = 16 * s + qd + 4 * e;
+        const uint32_t w = lds32(slot + c * 32 + 4 * r);
+        const float2 sm = lds64f(kmeta + c * 8);
+        const float2 sc = make_float2(sm.x, sm.x), lo = make_float2(sm.y, sm.y);
+        if constexpr (BITS == 8) {
+          float2 x0 = make_float2(byte_magic<0>(w), byte_magic<1>(w));
+          float2 x1 = make_float2(byte_magic<2>(w), byte_magic<3>(w));
+          x0 = __fadd2_rn(x0, make_float2(-kMagic, -kMagic));
+          x1 = __fadd2_rn(x1, make_float2(-kMagic, -kMagic));
+          x0 = __ffma2_rn(x0, sc, lo);
+          x1 = __ffma2_rn(x1, sc, lo);
+          f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
+        } else {
+          // byte b holds tokens 2b (low nibble) and 2b+1 (high nibble)
+          const uint32_t lo4 = w & 0x0F0F0F0Fu, hi4 = (w >> 4) & 0x0F0F0F0Fu;
+          float2 x0 = make_float2(byte_magic<0>(lo4), byte_magic<0>(hi4));
+          float2 x1 = make_float2(byte_magic<1>(lo4), byte_magic<1>(hi4));
+          float2 x2 = make_float2(byte_magic<2>(lo4), byte_magic<2>(hi4));
+          float2 x3 = make_float2(byte_magic<3>(lo4), byte_magic<3>(hi4));
+          const float2 mg = make_float2(-kMagic, -kMagic);
+          x0 = __ffma2_rn(__fadd2_rn(x0, mg), sc, lo);
+          x1 = __ffma2_rn(__fadd2_rn(x1, mg), sc, lo);
+          x2 = __ffma2_rn(__fadd2_rn(x2, mg), sc, lo);
+          x3 = __ffma2_rn(__fadd2_rn(x3, mg), sc, lo);
+          f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
+          f[e][4] = x2.x; f[e][5] = x2.y; f[e][6] = x3.x; f[e][7] = x3.y;
+        }
       }
       uint2 b[NT];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(qf + ((s * NT + nt) * 32 + lane) * 8);
+      for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(qfp + ((s * NT + nt) * 32 + lane) * 8);
 #pragma unroll
-      for (int mt = 0; mt < C::MTW; ++mt) {
-        // m-tile mt: row r <-> token TPL*r+2mt, row r+8 <-> token TPL*r+2mt+1
-        float2 x[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if constexpr (BITS == 8) {
-            x[e] = mt ? make_float2(byte_magic<2>(w[e]), byte_magic<3>(w[e]))
-                      : make_float2(byte_magic<0>(w[e]), byte_magic<1>(w[e]));
-          } else {
-            // byte mt holds token 2mt (low nibble) and 2mt+1 (high nibble)
-            const uint32_t lo4 = w[e] & 0x0F0F0F0Fu, hi4 = (w[e] >> 4) & 0x0F0F0F0Fu;
-            const uint32_t sel = 0x7440u | mt;
-            x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
-                               __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
-          }
-          x[e] = __ffma2_rn(__fadd2_rn(x[e], make_float2(-kMagic, -kMagic)), sc[e], lo[e]);
-        }
+      for (int mt = 0; mt < C::MTQ; ++mt) {
+        // m-tile mt: row r <-> lane token 2mt, row r+8 <-> lane token 2mt+1
         uint32_t a[4];
-        a[0] = E::pack2(x[0].x, x[1].x);
-        a[1] = E::pack2(x[0].y, x[1].y);
-        a[2] = E::pack2(x[2].x, x[3].x);
-        a[3] = E::pack2(x[2].y, x[3].y);
+        a[0] = E::pack2(f[0][2 * mt], f[1][2 * mt]);
+        a[1] = E::pack2(f[0][2 * mt + 1], f[1][2 * mt + 1]);
+        a[2] = E::pack2(f[2][2 * mt], f[3][2 * mt]);
+        a[3] = E::pack2(f[2][2 * mt + 1], f[3][2 * mt + 1]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816<DT>(S[mt][nt], a, b[nt].x, b[nt].y);
       }
     }
   }
 
-  // QK^T over residual key half h (16 tokens x D/2 channels) into S[0].
-  __device__ void qk_resid(uint32_t slot, int h) {
-    constexpr int STEPS = C::KSTEPS / 2;
-#pragma unroll 2
-    for (int sl = 0; sl < STEPS; ++sl) {
-      const int s = h * STEPS + sl;
-      const uint32_t col = (16 * sl + 2 * qd) * 2;
-      uint32_t a[4];
-      a[0] = lds32(slot + r * C::RKP + col);
-      a[1] = lds32(slot + (r + 8) * C::RKP + col);
-      a[2] = lds32(slot + r * C::RKP + col + 16);
-      a[3] = lds32(slot + (r + 8) * C::RKP + col + 16);
+  // QK^T over a residual K slot (16 tokens, one m-tile) -> S[0]
+  __device__ void qk_resid(uint32_t slot) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) S[0][nt][c] = 0.f;
+#pragma unroll 4
+    for (int s = 0; s < C::KSTEPS; ++s) {
+      const uint2 w0 = lds64(slot + r * C::RKP + (16 * s + 4 * qd) * 2);
+      const uint2 w1 = lds64(slot + (r + 8) * C::RKP + (16 * s + 4 * qd) * 2);
+      uint32_t a[4] = {w0.x, w1.x, w0.y, w1.y};
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint2 b = lds64(qf + ((s * NT + nt) * 32 + lane) * 8);
+        const uint2 b = lds64(qfr + ((s * NT + nt) * 32 + lane) * 8);
         mma16816<DT>(S[0][nt], a, b.x, b.y);
       }
     }
@@ -331,7 +325,7 @@ struct Warp {
   // ---------------------------------------------------------------------
   // Online softmax over the S tile; writes permuted P; rescales acc.
   //   MT       m-tiles in S
-  //   tok(m,h) token (item-local) of row r (h=0) / r+8 (h=1) of m-tile m
+  //   tok(m,h) token (slot-local) of row r (h=0) / r+8 (h=1) of m-tile m
   //   valid(t, row) mask (true for packed tokens)
   //   pos(t)   column of token t in the permuted P row
   // ---------------------------------------------------------------------
@@ -396,94 +390,102 @@ struct Warp {
   }
 
   // ---------------------------------------------------------------------
-  // P.V over packed value slot v (block tokens 16v..16v+15).
+  // P.V over a packed V slot of 32 tokens; kbase = first PV k-step of the
+  // slot within the current K slot's P row.
   // ---------------------------------------------------------------------
-  __device__ void pv_packed(uint32_t slot, int v) {
-    const uint32_t meta = slot + C::VT * C::VROWB;
-    uint2 b[NT];
+  __device__ void pv_packed(uint32_t slot, int kbase) {
+    const uint32_t meta = slot + 32 * C::VROWB;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      b[nt] = lds64(pbuf + (8 * nt + r) * PPITCH + (16 * v + 4 * qd) * 2);
+    for (int j = 0; j < 2; ++j) {
+      uint2 b[NT];
 #pragma unroll
-    for (int ch = 0; ch < C::NCH; ++ch) {
-      const int c0 = ch * 8 * C::CPL + C::CPL * r;   // lane's first channel in chunk
-      const int grp = c0 / 64;
-      constexpr int CB = C::CPL * BITS / 8;          // code bytes per token per chunk
-      uint32_t w[4][CB / 4 > 0 ? CB / 4 : 1];
-      float2 sc[4], lo[4];
+      for (int nt = 0; nt < NT; ++nt)
+        b[nt] = lds64(pbuf + (8 * nt + r) * PPITCH + (16 * (kbase + j) + 4 * qd) * 2);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        // k-index 2qd, 2qd+1, 2qd+8, 2qd+9 <-> slot token of the same index
-        const int t = 2 * qd + (e & 1) + 8 * (e >> 1);
-        const int off = c0 * BITS / 8;                 // byte of the lane's chunk in the row
-        const uint32_t addr =
-            slot + (off / C::VBOX) * C::VT * C::VBOX + swz<C::VSWZ>(t * C::VBOX + off % C::VBOX);
-        if constexpr (CB == 16) {
-          const uint4 x = lds128(addr);
-          w[e][0] = x.x; w[e][1] = x.y; w[e][2] = x.z; w[e][3] = x.w;
-        } else if constexpr (CB == 8) {
-          const uint2 x = lds64(addr);
-          w[e][0] = x.x; w[e][1] = x.y;
-        } else {
-          w[e][0] = lds32(addr);
-        }
-        const float2 sm = lds64f(meta + (t * C::NG + grp) * 8);
-        sc[e] = make_float2(sm.x, sm.x);
-        lo[e] = make_float2(sm.y, sm.y);
-      }
-#pragma unroll
-      for (int i = 0; i < C::MTC; ++i) {
-        // channels c0 + 2i (row r) and c0 + 2i + 1 (row r+8)
-        float2 x[4];
+      for (int ch = 0; ch < C::NCH; ++ch) {
+        const int c0 = ch * 8 * C::CPL + C::CPL * r;   // lane's first channel in chunk
+        const int grp = c0 / 64;
+        constexpr int CB = C::CPL * BITS / 8;           // code bytes per token per chunk
+        uint32_t w[4][CB / 4 > 0 ? CB / 4 : 1];
+        float2 sc[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          if constexpr (BITS == 8) {
-            const uint32_t word = w[e][i >> 1];
-            x[e] = (i & 1) ? make_float2(byte_magic<2>(word), byte_magic<3>(word))
-                           : make_float2(byte_magic<0>(word), byte_magic<1>(word));
+          // k-index 2qd, 2qd+1, 2qd+8, 2qd+9 <-> slot token 16j + the same
+          const int t = 16 * j + 2 * qd + (e & 1) + 8 * (e >> 1);
+          const int off = c0 * BITS / 8;                 // byte of the lane's chunk in the row
+          const uint32_t addr = slot + (off / C::VBOX) * 32 * C::VBOX +
+                                swz<C::VSWZ>(t * C::VBOX + off % C::VBOX);
+          if constexpr (CB == 16) {
+            uint4 v = lds128(addr);
+            w[e][0] = v.x; w[e][1] = v.y; w[e][2] = v.z; w[e][3] = v.w;
+          } else if constexpr (CB == 8) {
+            uint2 v = lds64(addr);
+            w[e][0] = v.x; w[e][1] = v.y;
           } else {
-            const uint32_t word = w[e][i >> 2];
-            const uint32_t lo4 = word & 0x0F0F0F0Fu, hi4 = (word >> 4) & 0x0F0F0F0Fu;
-            const uint32_t sel = 0x7440u | (i & 3);
-            x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
-                               __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
+            w[e][0] = lds32(addr);
           }
-          x[e] = __ffma2_rn(__fadd2_rn(x[e], make_float2(-kMagic, -kMagic)), sc[e], lo[e]);
+          const float2 sm = lds64f(meta + (t * C::NG + grp) * 8);
+          sc[e] = make_float2(sm.x, sm.x);
+          lo[e] = make_float2(sm.y, sm.y);
         }
-        uint32_t a[4];
-        a[0] = E::pack2(x[0].x, x[1].x);
-        a[1] = E::pack2(x[0].y, x[1].y);
-        a[2] = E::pack2(x[2].x, x[3].x);
-        a[3] = E::pack2(x[2].y, x[3].y);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816<DT>(acc[ch * C::MTC + i][nt], a, b[nt].x, b[nt].y);
+        for (int i = 0; i < C::MTC; ++i) {
+          // channels c0 + 2i (row r) and c0 + 2i + 1 (row r+8)
+          float2 x[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if constexpr (BITS == 8) {
+              const uint32_t word = w[e][i >> 1];
+              x[e] = (i & 1) ? make_float2(byte_magic<2>(word), byte_magic<3>(word))
+                             : make_float2(byte_magic<0>(word), byte_magic<1>(word));
+            } else {
+              const uint32_t word = w[e][i >> 2];
+              const uint32_t lo4 = word & 0x0F0F0F0Fu, hi4 = (word >> 4) & 0x0F0F0F0Fu;
+              const int bsel = i & 3;
+              const uint32_t sel = 0x7440u | bsel;
+              x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
+                                 __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
+            }
+            x[e] = __ffma2_rn(__fadd2_rn(x[e], make_float2(-kMagic, -kMagic)), sc[e], lo[e]);
+          }
+          uint32_t a[4];
+          a[0] = E::pack2(x[0].x, x[1].x);
+          a[1] = E::pack2(x[0].y, x[1].y);
+          a[2] = E::pack2(x[2].x, x[3].x);
+          a[3] = E::pack2(x[2].y, x[3].y);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma16816<DT>(acc[ch * C::MTC + i][nt], a, b[nt].x, b[nt].y);
+        }
       }
     }
   }
 
-  // P.V over residual value half h (item tokens 8h..8h+7, exact values).
-  __device__ void pv_resid(uint32_t slot, int h) {
+  // P.V over a residual V slot (16 tokens, exact values).
+  __device__ void pv_resid(uint32_t slot) {
     uint2 b[NT];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(pbuf + (8 * nt + r) * PPITCH + 4 * qd * 2);
-    const int t0 = resid_token<C::CPL>(qd, 2 * h) - 8 * h;
-    const int t1 = resid_token<C::CPL>(qd, 2 * h + 1) - 8 * h;
 #pragma unroll
     for (int ch = 0; ch < C::NCH; ++ch) {
       const int c0 = ch * 8 * C::CPL + C::CPL * r;
 #pragma unroll
       for (int piece = 0; piece < C::CPL / 8; ++piece) {
-        const uint4 w0 = lds128(slot + t0 * C::RVP + (c0 + 8 * piece) * 2);
-        const uint4 w1 = lds128(slot + t1 * C::RVP + (c0 + 8 * piece) * 2);
+        uint4 w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = resid_token<C::CPL>(qd, e);
+          w[e] = lds128(slot + t * C::RVP + (c0 + 8 * piece) * 2);
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint32_t x0 = (&w0.x)[k], x1 = (&w1.x)[k];
-          const uint32_t lo = prmt(x0, x1, 0x5410u), hi = prmt(x0, x1, 0x7632u);
+          const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k],
+                         w3 = (&w[3].x)[k];
           uint32_t a[4];
-          a[0] = h ? 0u : lo;
-          a[1] = h ? 0u : hi;
-          a[2] = h ? lo : 0u;
-          a[3] = h ? hi : 0u;
+          a[0] = prmt(w0, w1, 0x5410u);
+          a[1] = prmt(w0, w1, 0x7632u);
+          a[2] = prmt(w2, w3, 0x5410u);
+          a[3] = prmt(w2, w3, 0x7632u);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
             mma16816<DT>(acc[ch * C::MTC + piece * 4 + k][nt], a, b[nt].x, b[nt].y);
