@@ -306,9 +306,11 @@ def b200_arm(args, world, rank, local):
     torch.cuda.synchronize()
     clocks.start()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push('timed')      # lets a profiler keep to the timed launches
     start.record()
     launches = run_steps(seq, decode, args.steps)
     stop.record()
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     clk = clocks.stop()
     barrier(world)
