@@ -177,6 +177,31 @@ int ckv_attention_error(const void *workspace, int *flag, ckv_stream_t stream);
 int ckv_attention(const ckv_attn_args *args, void *workspace, size_t workspace_bytes,
                   ckv_stream_t stream);
 
+/* Size of the library's own scratch buffer used by ckv_attention_static. */
+#define CKV_STATIC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * ckv_attention without a caller workspace, for callers that may not
+ * allocate device memory where they call it: a host function enqueued on a
+ * stream, an allocator or memory-pool hook (allocating there re-enters the
+ * allocator), or an embedding runtime that owns every device allocation and
+ * hands out none for scratch.  Same arguments and results as ckv_attention;
+ * the split records and merge tickets go to a CKV_STATIC_SCRATCH_BYTES
+ * (4 MiB) array inside the library instead, so the call allocates nothing.
+ * Each device that loads the library holds its own copy of that array until
+ * the process exits.  A request whose ckv_attention_workspace() exceeds
+ * CKV_STATIC_SCRATCH_BYTES returns CKV_ERR_WORKSPACE before any GPU work.
+ * The ticket area is cleared on the stream at every call.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.
+ * Every call on one device uses the same array: two calls whose kernels can
+ * overlap on the GPU (different streams without ordering between them) race
+ * and give wrong results, so the caller must serialise them.  The give-up
+ * flag that ckv_attention_error reads is not exposed for this array.
+ * No counterpart in the reference.
+ */
+int ckv_attention_static(const ckv_attn_args *args, ckv_stream_t stream);
+
 /* Row index of (query head hq, position n) in a partial buffer. */
 static inline int64_t ckv_partial_row(int hq, int n, int nq) { return (int64_t)hq * nq + n; }
 
