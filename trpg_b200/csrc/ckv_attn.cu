@@ -21,15 +21,33 @@ constexpr int kMaxHeadsKV = 128;
 constexpr size_t kCounterOff = 256;
 constexpr size_t kCounterBytes = kCounterOff + size_t(CKV_MAX_SEQS) * kMaxHeadsKV * 4;
 
+// Bounded wait on an mbarrier phase that also gives up as soon as another
+// warp of the CTA has flagged an abort.  Returns false on either.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort || clock64() - start > (1ll << 31)) return false;
+  }
+  return true;
+}
+
 template <int BITS, int D, int NT, int DT, int MAXS>
 __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant__ Params<MAXS> p) {
   using C = Cfg<BITS, D, NT>;
   using T = typename Elem<DT>::T;
+  constexpr int NV = C::NV;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int s_seq, s_last;
-  __shared__ __align__(8) uint64_t s_bar[WARPS][2];
-  // 1024-byte aligned base: the 128-byte TMA swizzle needs aligned slots.
+  __shared__ volatile int s_abort;
+  // kfull[NK] kempty[NK] vfull[NV] vempty[NV] pfull[TEAMS][2] pempty[TEAMS][2]
+  __shared__ __align__(8) uint64_t s_bar[2 * NK + 2 * NV + 4 * TEAMS];
+  // 1024-byte aligned base: the TMA swizzle patterns repeat every 1024 bytes.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const uint32_t sbase = smem_u32(smem);
+  auto bar = [&](int i) { return smem_u32(&s_bar[i]); };
+  constexpr int KFULL = 0, KEMPTY = NK, VFULL = 2 * NK, VEMPTY = 2 * NK + NV,
+                PFULL = 2 * NK + 2 * NV, PEMPTY = PFULL + 2 * TEAMS;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
@@ -40,186 +58,361 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       if (p.seq[mid].cta_begin <= cta) lo = mid; else hi = mid - 1;
     }
     s_seq = lo;
+    s_abort = 0;
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(bar(KFULL + i), 1);
+      mbar_init(bar(KEMPTY + i), TEAM_THREADS);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(bar(VFULL + i), 1);
+      mbar_init(bar(VEMPTY + i), TEAM_THREADS);
+    }
+    for (int i = 0; i < 2 * TEAMS; ++i) {
+      mbar_init(bar(PFULL + i), TEAM_THREADS);
+      mbar_init(bar(PEMPTY + i), TEAM_THREADS);
+    }
+    mbar_fence_init();
   }
   __syncthreads();
+  if (tid == PRODUCER * 32) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.seq[s_seq].tk) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.seq[s_seq].tv) : "memory");
+  }
   const int seq = s_seq;
   const SeqDev &sd = p.seq[seq];
   const int local = cta - sd.cta_begin;
   const int head = local / sd.cph, split = local % sd.cph;
   const int G = p.group, rows = p.rows, nq = p.nq;
 
-  // ---- query fragments for both channel orders -----------------------------
-  const uint32_t qfp = smem_u32(smem), qfr = qfp + C::QFRAG;
-  const uint32_t bar0 = smem_u32(&s_bar[warp][0]), bar1 = smem_u32(&s_bar[warp][1]);
-  if (lane == 0) {
-    mbar_init(bar0, 1);
-    mbar_init(bar1, 1);
-    mbar_fence_init();
-  }
-  {
-    const uint16_t *q = static_cast<const uint16_t *>(sd.q);
-    for (int x = tid; x < C::KSTEPS * NT * 32; x += THREADS) {
+  // Query B fragments (channel order of the MMA k index), filled by the QK
+  // warps while the producers start streaming.
+  if (warp < QK_WARPS) {
+    const uint16_t *qb = static_cast<const uint16_t *>(sd.q);
+    for (int x = tid; x < C::KQS * NT * 32; x += QK_WARPS * 32) {
       const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
-      const int rr = ln >> 2, qq = ln & 3, row = 8 * nt + rr;
-      uint2 vp = make_uint2(0, 0), vr = make_uint2(0, 0);
+      const int row = 8 * nt + (ln >> 2), cb = 16 * s + 2 * (ln & 3);
+      uint2 v = make_uint2(0, 0);
       if (row < rows) {
-        const int n = row / G, g = row % G;
-        const uint16_t *qrow = q + (head * G + g) * sd.q_h + n * sd.q_n;
-        const int cp = 16 * s + qq, cr = 16 * s + 4 * qq;
-        vp.x = qrow[cp] | (uint32_t(qrow[cp + 4]) << 16);
-        vp.y = qrow[cp + 8] | (uint32_t(qrow[cp + 12]) << 16);
-        vr.x = qrow[cr] | (uint32_t(qrow[cr + 1]) << 16);
-        vr.y = qrow[cr + 2] | (uint32_t(qrow[cr + 3]) << 16);
+        const uint16_t *qrow = qb + (head * G + row % G) * sd.q_h + (row / G) * sd.q_n;
+        v.x = qrow[cb] | (uint32_t(qrow[cb + 1]) << 16);
+        v.y = qrow[cb + 8] | (uint32_t(qrow[cb + 9]) << 16);
       }
-      *reinterpret_cast<uint2 *>(smem + x * 8) = vp;
-      *reinterpret_cast<uint2 *>(smem + C::QFRAG + x * 8) = vr;
+      *reinterpret_cast<uint2 *>(smem + C::OFF_Q + x * 8) = v;
     }
+    named_sync(BAR_QFRAG, QK_WARPS * 32);
   }
-  __syncthreads();
 
-  // ---- this warp's work items ---------------------------------------------
+  // This CTA's items: packed units [ub, ue) then residual chunks of RCHUNK tokens.
   const int np = sd.ue - sd.ub;
-  const int nr = (sd.re - sd.rb + 15) / 16;
+  const int nr = (sd.re - sd.rb + RCHUNK - 1) / RCHUNK;
   const int ni = np + nr;
   const int ib = int(int64_t(split) * ni / sd.cph);
-  const int ie = int(int64_t(split + 1) * ni / sd.cph);
-  const int first = ib + warp;
-  const int kt = ie > first ? (ie - first + WARPS - 1) / WARPS : 0;
-  const int pend = ie < np ? ie : np;
-  const int kp = pend > first ? (pend - first + WARPS - 1) / WARPS : 0;
-  const int total = kp * C::SPB + (kt - kp) * 2;
-
-  Warp<BITS, D, NT, DT> w;
-  w.init(lane, qfp, qfr, qfp + C::QFRAG_AL + warp * C::WARP_BYTES, p.scale_log2);
-
-  const T *rk = static_cast<const T *>(sd.rk) + head * sd.rk_h;
-  const T *rv = static_cast<const T *>(sd.rv) + head * sd.rv_h;
-  const int length = sd.length, packed = sd.packed;
-
-  auto is_tma = [&](int s) { return s < kp * C::SPB; };
-  auto issue = [&](int s) {
-    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
-    const uint32_t bar = (s & 1) ? bar1 : bar0;
-    if (is_tma(s)) {
-      const int k = s / C::SPB, part = s % C::SPB;
-      const int unit = sd.ub + first + k * WARPS;
-      const int qq = part / (1 + C::VSQ), sub = part % (1 + C::VSQ);
-      if (sub == 0)
-        w.load_packed_k(sd, head, unit, qq, slot, qq == 0, bar);
-      else
-        w.load_packed_v(sd, head, unit * 128 + qq * C::QT + (sub - 1) * 32, slot, bar);
-    } else {
-      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
-      const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
-      if (part == 0)
-        w.load_resid(rk, sd.rk_t, t0, sd.re, slot, C::RKP);
-      else
-        w.load_resid(rv, sd.rv_t, t0, sd.re, slot, C::RVP);
-    }
+  const int n = int(int64_t(split + 1) * ni / sd.cph) - ib;
+  auto fail = [&]() {
+    atomicOr(p.error, 1u);
+    s_abort = 1;
   };
 
-  const int rr = lane >> 2;
-  auto compute = [&](int s) {
-    const uint32_t slot = w.ring + (s & 1) * C::SLOT;
-    if (is_tma(s)) {
-      const int part = s % C::SPB;
-      const int sub = part % (1 + C::VSQ);
-      if (sub == 0) {
-        w.qk_packed(slot);
-        w.template softmax<C::MTQ>(
-            [&](int mt, int h) { return C::TPL * rr + 2 * mt + h; },
-            [](int, int) { return true; }, [](int t) { return packed_pos(t); });
-      } else {
-        w.pv_packed(slot, 2 * (sub - 1));
-      }
-    } else {
-      const int k = (s - kp * C::SPB) >> 1, part = (s - kp * C::SPB) & 1;
-      if (part == 0) {
-        const int t0 = sd.rb + (first + (kp + k) * WARPS - np) * 16;
-        w.qk_resid(slot);
-        w.template softmax<1>(
-            [&](int, int h) { return rr + 8 * h; },
-            [&](int t, int row) {
-              const int ri = t0 + t;
-              return ri < sd.re && (nq == 1 || packed + ri <= length - nq + row / G);
-            },
-            [](int t) { return resid_pos<C::CPL>(t); });
-      } else {
-        w.pv_resid(slot);
-      }
-    }
-  };
+  const int r = lane >> 2, qd = lane & 3;
+  const int team = warp < QK_WARPS ? warp / TEAM_WARPS : (warp - QK_WARPS) / TEAM_WARPS;
+  float m_run[NT][2], l_run[NT][2];
+  float O[C::MTV][NT][4];
 
-  // Every slot commits one cp.async group (empty for TMA slots), so the
-  // residual slots can wait with cp.async.wait_group 1; TMA slots wait on
-  // their mbarrier phase.
-  uint32_t phase = 0;  // bit k: parity of the next completion of ring slot k
-  __syncwarp();
-  if (total > 0) issue(0);
-  cp_async_commit();
-  if (total > 1) issue(1);
-  cp_async_commit();
-  int s = 0;
-  for (; s < total; ++s) {
-    if (is_tma(s)) {
-      const int k = s & 1;
-      if (!mbar_wait(k ? bar1 : bar0, (phase >> k) & 1)) {
-        if (lane == 0) atomicOr(p.error, 1u);
-        break;
+  if (warp >= PRODUCER) {
+    // ---- producers: warp PRODUCER streams K stages, PRODUCER + 1 V stages -------
+    const bool kchain = warp == PRODUCER;
+    const int depth = kchain ? NK : NV;
+    const int full0 = kchain ? KFULL : VFULL, empty0 = kchain ? KEMPTY : VEMPTY;
+    const int stage_bytes = kchain ? C::KST : C::VST;
+    const uint32_t ring = sbase + (kchain ? C::OFF_K : C::OFF_V);
+    const T *res = static_cast<const T *>(kchain ? sd.rk : sd.rv);
+    const int64_t res_h = kchain ? sd.rk_h : sd.rv_h, res_t = kchain ? sd.rk_t : sd.rv_t;
+    int issued = 0;
+    for (int i = 0; i < n; ++i) {
+      const int st = i % depth;
+      // One lane decides for the warp so that all lanes take the same path.
+      int go = 0;
+      if (lane == 0) {
+        go = !s_abort;
+        if (go && i >= depth && !wait_or_abort(bar(empty0 + st), ((i / depth) & 1) ^ 1, &s_abort)) {
+          fail();
+          go = 0;
+        }
       }
-      phase ^= 1u << k;
-    } else {
-      cp_async_wait<1>();
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      const uint32_t dst = ring + st * stage_bytes, fb = bar(full0 + st);
+      const int it = ib + i;
+      if (it < np) {
+        if (lane == 0) {
+          const int unit = sd.ub + it;
+          if (kchain) {
+            mbar_expect_tx(fb, C::KCODE + C::KMETA);
+            tma_load_4d(dst, &sd.tk, fb, 0, 0, unit, head);
+            bulk_load(dst + C::KCODE, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, fb);
+          } else {
+            mbar_expect_tx(fb, C::VCODE + C::VMETA);
+#pragma unroll
+            for (int bx = 0; bx < C::NVB; ++bx)
+              tma_load_3d(dst + bx * 128 * C::VBOX, &sd.tv, fb, bx * C::VBOX, unit * 128, head);
+            bulk_load(dst + C::VCODE, sd.vm + head * sd.vm_h + int64_t(unit) * 128 * sd.vm_t, C::VMETA,
+                      fb);
+          }
+        }
+      } else {
+        // Residual chunk: 16-byte cp.async by every lane into rows of pitch
+        // RP.  Rows past the window's end repeat its last token (finite
+        // values, masked out of the softmax).
+        const int t0 = sd.rb + (it - np) * RCHUNK;
+        const int cnt = min(RCHUNK, sd.re - t0);
+        const T *src = res + head * res_h;
+        constexpr int CH = 2 * D / 16;   // 16-byte pieces per row
+        for (int x = lane; x < RCHUNK * CH; x += 32) {
+          const int t = x / CH, k = x % CH;
+          const int ts = t < cnt ? t : cnt - 1;
+          cp_async16(dst + t * C::RP + k * 16, src + int64_t(t0 + ts) * res_t + k * 8);
+        }
+        cp_async_mbar_arrive(fb);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(fb);
+      }
+      __syncwarp();
+      issued = i + 1;
     }
-    __syncwarp();
-    compute(s);
-    __syncwarp();
-    if (s + 2 < total) issue(s + 2);
+    // Let every issued copy land before the stage memory is reused.
     cp_async_commit();
-  }
-  if (s < total) {
-    // A wait gave up: let the copies still in flight land (bounded) before
-    // this CTA's shared memory is reused or released.
-    for (int k2 = s; k2 < s + 2 && k2 < total; ++k2)
-      if (is_tma(k2)) mbar_wait((k2 & 1) ? bar1 : bar0, (phase >> (k2 & 1)) & 1);
-  }
-  cp_async_wait<0>();
-
-  // ---- warp -> CTA merge ----------------------------------------------------
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float v = w.l[nt][j];
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      v += __shfl_xor_sync(0xffffffffu, v, 8);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      w.l[nt][j] = v;
+    cp_async_wait<0>();
+    if (lane == 0) {
+      for (int st = 0; st < depth && st < issued; ++st) {
+        const int last = st + (issued - 1 - st) / depth * depth;
+        mbar_wait(bar(full0 + st), (last / depth) & 1);
+      }
     }
-  __syncthreads();  // ring memory becomes merge scratch
-  constexpr int WR = 8 * NT;  // rows held by a warp
-  float *mrg = reinterpret_cast<float *>(smem + C::QFRAG_AL);
-  float *ml = mrg + WARPS * WR * D;
-  {
-    float *mw = mrg + warp * WR * D;
+    __syncwarp();
+  } else if (warp < QK_WARPS) {
+    // ---- QK warps: team `team`, token quarter q ------------------------------------
+    QkWarp<BITS, D, NT, DT> qw;
+    qw.lane = lane; qw.r = r; qw.qd = qd; qw.q = warp % TEAM_WARPS;
+    qw.qfr = smem + C::OFF_Q;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        m_run[nt][j] = -INFINITY;   // this warp's P scale m_q (integer valued)
+        l_run[nt][j] = 0.f;
+      }
+    const float sl = p.scale_log2;
+    for (int i = team; i < n; i += TEAMS) {
+      const int k = i >> 1, par = k & 1;
+      const int st = i % NK;
+      const int it = ib + i;
+      const bool pk = it < np;
+      float S[2][NT][4];
+      const bool have = !s_abort && wait_or_abort(bar(KFULL + st), (i / NK) & 1, &s_abort);
+      if (!have && !s_abort) fail();
+      if (have) {
+        if (pk) qw.packed(smem + C::OFF_K + st * C::KST, S);
+        else qw.resid(sbase + C::OFF_K + st * C::KST, S[0]);
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) S[mt][nt][c] = 0.f;
+      }
+      mbar_arrive(bar(KEMPTY + st));
+
+      // Scale and mask; S[mt][nt][2u + j] is token tok(mt, u), query row 8nt + 2qd + j.
+      const int rbase = sd.rb + (it - np) * RCHUNK;   // residual window index of chunk token 0
+      float muse[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int row = 8 * nt + 2 * qd + j;
+          float m = -INFINITY;
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              float x = S[mt][nt][2 * u + j] * sl;
+              if (!pk) {
+                const int ri = rbase + 16 * qw.q + r + 8 * u;
+                const bool ok = mt == 0 && ri < sd.re &&
+                                (nq == 1 || sd.packed + ri <= sd.length - nq + row / G);
+                if (!ok) x = -INFINITY;
+              }
+              S[mt][nt][2 * u + j] = x;
+              m = fmaxf(m, x);
+            }
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+          // Raise this warp's scale to the next integer above the new maximum.
+          const float mold = m_run[nt][j];
+          const float mnew = m > mold ? ceilf(m) : mold;
+          l_run[nt][j] *= pow2i(mold - mnew);
+          m_run[nt][j] = mnew;
+          muse[nt][j] = mnew == -INFINITY ? 0.f : mnew;
+        }
+      if (k >= 2 && !s_abort &&
+          !wait_or_abort(bar(PEMPTY + team * 2 + par), ((k >> 1) & 1) ^ 1, &s_abort))
+        fail();
+      uint8_t *pb = smem + C::OFF_P + (team * 2 + par) * C::ROWS * PP;
+      float *ms = reinterpret_cast<float *>(smem + C::OFF_XM) + ((team * 2 + par) * TEAM_WARPS + qw.q) * C::ROWS;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int row = 8 * nt + 2 * qd + j;
+          float sum = 0.f;
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (!pk && mt == 1) continue;
+              const float pv = ex2(S[mt][nt][2 * u + j] - muse[nt][j]);
+              sum += pv;
+              const int t = pk ? 32 * qw.q + 4 * r + 2 * mt + u : 16 * qw.q + r + 8 * u;
+              *reinterpret_cast<T *>(pb + row * PP + ppos(t) * 2) = Elem<DT>::from_f32(pv);
+            }
+          l_run[nt][j] += sum;
+          if (r == 0) ms[row] = m_run[nt][j];
+        }
+      mbar_arrive(bar(PFULL + team * 2 + par));
+    }
+  } else {
+    // ---- PV warps: team `team`, channel quarter c ----------------------------------
+    PvWarp<BITS, D, NT, DT> pw;
+    pw.lane = lane; pw.r = r; pw.qd = qd; pw.c = (warp - QK_WARPS) % TEAM_WARPS;
 #pragma unroll
     for (int i = 0; i < C::MTV; ++i)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int row = 8 * nt + 2 * w.qd + (c & 1);
-          mw[row * D + w.out_channel(i, c)] = w.acc[i][nt][c];
+        for (int c = 0; c < 4; ++c) O[i][nt][c] = 0.f;
+    // Common scale of this team's accumulator: rows 8nt + 2qd + j (the
+    // accumulator columns) and rows 8nt + r (the P fragment columns).
+    float Mc[NT][2], Mb[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      Mc[nt][0] = Mc[nt][1] = Mb[nt] = -INFINITY;
+    }
+    for (int i = team; i < n; i += TEAMS) {
+      const int k = i >> 1, par = k & 1;
+      const int sv = i % NV;
+      const bool pk = ib + i < np;
+      bool ok = !s_abort && wait_or_abort(bar(VFULL + sv), (i / NV) & 1, &s_abort);
+      ok = ok && wait_or_abort(bar(PFULL + team * 2 + par), (k >> 1) & 1, &s_abort);
+      if (!ok && !s_abort) fail();
+      if (ok) {
+        const float *ms = reinterpret_cast<const float *>(smem + C::OFF_XM) + (team * 2 + par) * TEAM_WARPS * C::ROWS;
+        // Accumulator rescale: new common scale per accumulator column.
+        bool unit = true;
+        float2 a2[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float mx0 = Mc[nt][0], mx1 = Mc[nt][1];
+#pragma unroll
+          for (int w = 0; w < TEAM_WARPS; ++w) {
+            const float2 v = *reinterpret_cast<const float2 *>(ms + w * C::ROWS + 8 * nt + 2 * qd);
+            mx0 = fmaxf(mx0, v.x);
+            mx1 = fmaxf(mx1, v.y);
+          }
+          a2[nt] = make_float2(pow2i(Mc[nt][0] - mx0), pow2i(Mc[nt][1] - mx1));
+          unit = unit && (mx0 == Mc[nt][0]) && (mx1 == Mc[nt][1]);
+          Mc[nt][0] = mx0;
+          Mc[nt][1] = mx1;
         }
-    if (w.r == 0) {
+        if (!__all_sync(0xffffffffu, unit)) {
+#pragma unroll
+          for (int m = 0; m < C::MTV; ++m)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              float2 x0 = __fmul2_rn(make_float2(O[m][nt][0], O[m][nt][1]), a2[nt]);
+              float2 x1 = __fmul2_rn(make_float2(O[m][nt][2], O[m][nt][3]), a2[nt]);
+              O[m][nt][0] = x0.x; O[m][nt][1] = x0.y; O[m][nt][2] = x1.x; O[m][nt][3] = x1.y;
+            }
+        }
+        // P fragment factors 2^(m_q - M) for the fragment column row 8nt + r.
+        uint32_t fb[TEAM_WARPS][NT];
+        bool same = true;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float mq[TEAM_WARPS];
+          float mx = Mb[nt];
+#pragma unroll
+          for (int w = 0; w < TEAM_WARPS; ++w) {
+            mq[w] = ms[w * C::ROWS + 8 * nt + r];
+            mx = fmaxf(mx, mq[w]);
+          }
+          Mb[nt] = mx;
+#pragma unroll
+          for (int w = 0; w < TEAM_WARPS; ++w) {
+            const float f = pow2i(mq[w] - mx);
+            same = same && mq[w] == mx;
+            fb[w][nt] = Elem<DT>::pack2(f, f);
+          }
+        }
+        const bool scaled = !__all_sync(0xffffffffu, same);
+        const uint8_t *vst = smem + C::OFF_V + sv * C::VST;
+        const uint8_t *pb = smem + C::OFF_P + (team * 2 + par) * C::ROWS * PP;
+        if (pk) pw.packed(vst, pb, O, fb, scaled);
+        else pw.resid(vst, pb, O, fb, scaled);
+      }
+      mbar_arrive(bar(VEMPTY + sv));
+      mbar_arrive(bar(PEMPTY + team * 2 + par));
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = Mc[nt][0];
+      m_run[nt][1] = Mc[nt][1];
+    }
+  }
+  __syncthreads();
+
+  // ---- CTA record: merge the two teams' states ----------------------------------
+  // Stage memory is free now.  red[t][row][d]: team t's accumulator at its
+  // common scale M_t; lred[t][q][row] / lms[t][q][row]: QK warp q's row sum
+  // and its scale m_q; mrow[t][row] = M_t.
+  float *red = reinterpret_cast<float *>(smem);          // [TEAMS][ROWS][D]
+  float *lred = red + TEAMS * C::ROWS * D;               // [TEAMS][4][ROWS]
+  float *lms = lred + TEAMS * TEAM_WARPS * C::ROWS;      // [TEAMS][4][ROWS]
+  float *mrow = lms + TEAMS * TEAM_WARPS * C::ROWS;      // [TEAMS][ROWS]
+  if (warp < QK_WARPS) {
+    const int q = warp % TEAM_WARPS;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float v = l_run[nt][j];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if (r == 0) {
+          const int row = 8 * nt + 2 * qd + j;
+          lred[(team * TEAM_WARPS + q) * C::ROWS + row] = v;
+          lms[(team * TEAM_WARPS + q) * C::ROWS + row] = m_run[nt][j];
+        }
+      }
+  } else if (warp < PRODUCER) {
+    const int c = (warp - QK_WARPS) % TEAM_WARPS;
+    float *rt = red + team * C::ROWS * D;
+#pragma unroll
+    for (int m = 0; m < C::MTV; ++m)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int row = 8 * nt + 2 * w.qd + j;
-          ml[(warp * WR + row) * 2] = w.m[nt][j];
-          ml[(warp * WR + row) * 2 + 1] = w.l[nt][j];
+        for (int cc = 0; cc < 4; ++cc) {
+          const int row = 8 * nt + 2 * qd + (cc & 1);
+          const int ch = (D / 4) * c + C::CPL * r + 2 * m + (cc >> 1);
+          rt[row * D + ch] = O[m][nt][cc];
         }
+    if (c == 0 && r == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) mrow[team * C::ROWS + 8 * nt + 2 * qd + j] = m_run[nt][j];
     }
   }
   __syncthreads();
@@ -227,23 +420,22 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   float *recml = p.rec_ml + size_t(cta) * rows * 2;
   for (int idx = tid; idx < rows * D; idx += THREADS) {
     const int row = idx / D, d = idx % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < WARPS; ++k) M = fmaxf(M, ml[(k * WR + row) * 2]);
-    float O = 0.f, L = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int k = 0; k < WARPS; ++k) {
-        const float mk = ml[(k * WR + row) * 2];
-        const float wt = mk == -INFINITY ? 0.f : ex2(mk - M);
-        O += wt * mrg[(k * WR + row) * D + d];
-        L += wt * ml[(k * WR + row) * 2 + 1];
-      }
-    }
-    rec[idx] = O;
+    const float m0 = mrow[row], m1 = mrow[C::ROWS + row];
+    const float M = fmaxf(m0, m1);
+    const float w0 = m0 == -INFINITY ? 0.f : ex2(m0 - M);
+    const float w1 = m1 == -INFINITY ? 0.f : ex2(m1 - M);
+    rec[idx] = red[row * D + d] * w0 + red[(C::ROWS + row) * D + d] * w1;
     if (d == 0) {
+      float L[TEAMS] = {0.f, 0.f};
+#pragma unroll
+      for (int t = 0; t < TEAMS; ++t)
+#pragma unroll
+        for (int w = 0; w < TEAM_WARPS; ++w) {
+          const int x = (t * TEAM_WARPS + w) * C::ROWS + row;
+          L[t] += lred[x] * pow2i(lms[x] - mrow[t * C::ROWS + row]);
+        }
       recml[row * 2] = M;
-      recml[row * 2 + 1] = L;
+      recml[row * 2 + 1] = L[0] * w0 + L[1] * w1;
     }
   }
   __threadfence();
@@ -261,9 +453,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   // records with many independent 16-byte loads in flight.
   const int c0 = sd.cta_begin + head * sd.cph;
   const int cph = sd.cph;
-  float *s_w = reinterpret_cast<float *>(smem + C::QFRAG_AL);  // [rows][cph] m, then weight
-  float *s_l = s_w + rows * cph;                                 // [rows][cph] l
-  float *s_row = s_l + rows * cph;                               // [rows] (M, L)
+  float *s_w = reinterpret_cast<float *>(smem);   // [rows][cph] m, then weight
+  float *s_l = s_w + rows * cph;                  // [rows][cph] l
+  float *s_row = s_l + rows * cph;                // [rows] (M, L)
   for (int idx = tid; idx < rows * cph; idx += THREADS) {
     const int row = idx / cph, c = idx % cph;
     const float2 ml2 =
@@ -316,8 +508,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
     }
     const float M = s_row[2 * row], L = s_row[2 * row + 1];
-    const int n = row / G, g = row % G;
-    const int64_t orow = int64_t(head * G + g) * nq + n;
+    const int nn = row / G, g = row % G;
+    const int64_t orow = int64_t(head * G + g) * nq + nn;
     if (p.partial) {
       float *o = static_cast<float *>(sd.out) + orow * (D + 2);
       o[4 * d4] = acc.x; o[4 * d4 + 1] = acc.y; o[4 * d4 + 2] = acc.z; o[4 * d4 + 3] = acc.w;
@@ -381,16 +573,19 @@ int sm_count() {
 }
 
 int seq_items(const ckv_seq &s) {
-  return (s.unit_end - s.unit_begin) + (s.resid_end - s.resid_begin + 15) / 16;
+  return (s.unit_end - s.unit_begin) + (s.resid_end - s.resid_begin + RCHUNK - 1) / RCHUNK;
 }
 
+constexpr int kItemsPerCta = 8;   // items (blocks / residual chunks) one CTA pipelines
+
 // CTAs per (sequence, KV head): a whole number of waves of one CTA per SM,
-// about two items per warp, shared out in proportion to each pair's items.
+// about kItemsPerCta items per CTA, shared out in proportion to each pair's
+// items.
 int make_plan(const ckv_attn_args &a, int D, Plan &pl) {
   const int sms = sm_count();
   int64_t total = 0;
   for (int i = 0; i < a.num_seqs; ++i) total += int64_t(seq_items(a.seqs[i])) * a.heads_kv;
-  const int64_t per_wave = int64_t(sms) * WARPS * 2;
+  const int64_t per_wave = int64_t(sms) * kItemsPerCta;
   const int64_t waves = std::max<int64_t>(1, (total + per_wave - 1) / per_wave);
   const int64_t target = int64_t(sms) * waves;
   int grid = 0;
@@ -494,10 +689,11 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   constexpr uint64_t S = 128 * BITS / 8;
   const cuuint64_t kdims[4] = {S, cuuint64_t(D), cuuint64_t(s.unit_end), cuuint64_t(hkv)};
   const cuuint64_t kstr[3] = {S, cuuint64_t(s.kd_stride_unit), cuuint64_t(s.kd_stride_head)};
-  const cuuint32_t kbox[4] = {32, cuuint32_t(D), 1, 1};
+  const cuuint32_t kbox[4] = {cuuint32_t(S), cuuint32_t(D), 1, 1};
   const cuuint32_t one[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle kswz = S == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = enc(&d.tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t *>(s.key_data), kdims,
-                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   kstr, kbox, one, CU_TENSOR_MAP_INTERLEAVE_NONE, kswz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("key tensor map rejected (bank strides)");
@@ -505,7 +701,7 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   }
   const cuuint64_t vdims[3] = {cuuint64_t(C::VROWB), cuuint64_t(s.unit_end) * 128, cuuint64_t(hkv)};
   const cuuint64_t vstr[2] = {cuuint64_t(s.vd_stride_token), cuuint64_t(s.vd_stride_head)};
-  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), 32, 1};
+  const cuuint32_t vbox[3] = {cuuint32_t(C::VBOX), 128, 1};
   const CUtensorMapSwizzle swz = C::VBOX == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : C::VBOX == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                  : CU_TENSOR_MAP_SWIZZLE_32B;

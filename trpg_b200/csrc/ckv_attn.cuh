@@ -1,19 +1,37 @@
 // Split-KV GQA attention over the compressed KV cache (sm_100a).
 //
-// One launch covers every (sequence, KV head) pair of a call.  Each pair is
-// split across `cph` CTAs; each CTA splits its share across WARPS warps; each
-// warp streams its own work items through a private two-slot ring in shared
-// memory and keeps its own online-softmax state.  Packed tiles arrive by TMA
-// (cp.async.bulk.tensor from per-sequence tensor maps, metadata by 1-D bulk
-// copies) signalled on one mbarrier per slot; the exact residual arrives by
-// 16-byte cp.async.  Warps merge inside the CTA, CTAs merge in the last CTA of
-// the pair (atomic ticket), all in one launch.
+// One launch covers every (sequence, KV head) pair of a call.  A pair's work
+// items -- packed 128-token blocks, then 64-token chunks of the exact
+// residual window -- are split into contiguous ranges, one per CTA; the CTAs
+// of a pair merge their partial results in the last CTA to finish (atomic
+// ticket), all in the same launch.
 //
-// Work items:
-//   packed block  -- 128 tokens of one KV head, consumed in "quarters" of
-//                    32 (Q8) or 64 (Q4) tokens: a K slot (all channels of the
-//                    quarter's tokens) then one or two V slots of 32 tokens.
-//   residual item -- 16 exact bf16/fp16 tokens of the recent window.
+// Inside a CTA the roles are specialised.  Two teams take alternate items
+// (team t owns items t, t+2, ...) with their own online-softmax state, so one
+// team's synchronisation latency is covered by the other team's arithmetic;
+// the two states merge once at the end.
+//
+//   2 producers    the K warp streams K stages (key codes by one TMA tile
+//                  copy, [D channels][128 tokens] bytes, 128/64-byte swizzle,
+//                  plus the block's (scale, low) by a 1-D bulk copy); the V
+//                  warp streams V stages ([128 tokens][D*bits/8] bytes in
+//                  boxes of up to 128 bytes, swizzled, plus per-token
+//                  metadata).  Residual chunks arrive by 16-byte cp.async from
+//                  all 32 lanes into padded rows.  Stages are rings of NK / NV
+//                  buffers guarded by full/empty mbarriers, shared by the
+//                  teams.
+//   4 QK warps     per team; warp q owns token quarter q of a block (32
+//                  tokens) over all channels: logits with mma.sync m16n8k16,
+//                  then P = 2^(s - m_q) (query dtype) into the team's double
+//                  buffer.  Each warp keeps its own running row maximum m_q,
+//                  rounded up to an integer so that moving between the
+//                  warps' scales is an exact power of two; the warps never
+//                  wait for each other.
+//   4 PV warps     per team; warp c owns channel quarter c (D/4 channels) over
+//                  all tokens of the item.  It takes the item's common scale
+//                  M = max(M, m_0..m_3), rescales its accumulator by 2^(M_old -
+//                  M) and each QK warp's P fragments by 2^(m_q - M), then
+//                  O += P.V.
 //
 // Numerics follow models/compressed_kv_kernels.py:_partial (:12-77): a code
 // is dequantized as fma(code, scale, low) and rounded to the query dtype
@@ -22,21 +40,11 @@
 // to the query dtype before P.V (:72) while the denominator sums the fp32
 // probabilities (:73); partials merge with 2^(m_s - max m) weights (:85-89).
 //
-// Tensor-core use: mma.sync m16n8k16 (bf16/fp16 in, fp32 accumulate) with
-// tokens or channels on M and the query rows (n, g) on N.  QK^T is
-// S^T[token][row] = K^T[token][channel] q^T[channel][row]; PV is
-// O^T[channel][row] = V^T[channel][token] P^T[token][row].  Codes are
-// dequantized straight into A fragments in registers.  Because the reduction
-// order inside an MMA is free, channels and tokens are permuted so that every
-// shared-memory read is conflict-free without a swizzle:
-//   * K slot rows are channels (32 bytes each); A-fragment k-index 2qd+e
-//     maps to channel 16s+qd+4e', so the four lanes of a row group read rows
-//     8 words apart.
-//   * V slot rows are tokens, loaded as 128-byte boxes with the TMA 128-byte
-//     swizzle (16-byte chunk c of row t lands at chunk c ^ (t & 7)); with the
-//     natural PV token order (k-index 2qd+b <-> token 2qd+b) the 8 lanes of a
-//     quarter-warp read 8 different chunks.
-//   * P is stored permuted so each lane's B fragment is one 8-byte load.
+// Tensor-core use is mma.sync m16n8k16 (bf16/fp16 in, fp32 accumulate) with
+// tokens (QK) or channels (PV) on M and the query rows (position n, group
+// member g) on N: the row count is at most 16, far too small for the
+// shared-memory operands of the 5th-generation MMA, while the dequantized
+// codes can go from registers straight into mma.sync fragments.
 #pragma once
 
 #include <cuda.h>
@@ -46,13 +54,22 @@
 namespace ckv {
 namespace attn {
 
-constexpr int WARPS = 8;
+constexpr int TEAMS = 2;
+constexpr int TEAM_WARPS = 4;                    // QK warps (and PV warps) per team
+constexpr int QK_WARPS = TEAMS * TEAM_WARPS;     // warps [0, 8): QK, team = w / 4
+constexpr int PV_WARPS = TEAMS * TEAM_WARPS;     // warps [8, 16): PV, team = (w - 8) / 4
+constexpr int PRODUCER = QK_WARPS + PV_WARPS;    // K producer warp; PRODUCER + 1: V
+constexpr int WARPS = PRODUCER + 2;
 constexpr int THREADS = WARPS * 32;
-constexpr int PPITCH = 160;          // bytes per P row (<= 64 tokens), 40 words
+constexpr int TEAM_THREADS = TEAM_WARPS * 32;
+constexpr int RCHUNK = 64;                       // residual tokens per work item
+constexpr int NK = 3;                            // K stage ring depth
+constexpr int PP = 288;                          // P row pitch: 128 tokens + 16-byte pad
+constexpr int BAR_QFRAG = 1;                     // named barrier of the QK warps (query fragments)
 
 struct alignas(64) SeqDev {
-  CUtensorMap tk;   // key codes   [H][units][D][S] bytes, box 32 bytes x D channels
-  CUtensorMap tv;   // value codes [H][tokens][D*bits/8] bytes, box VBOX bytes x 32 tokens
+  CUtensorMap tk;   // key codes   [H][units][D][S] bytes, box S bytes x D channels
+  CUtensorMap tv;   // value codes [H][tokens][D*bits/8] bytes, box VBOX bytes x 128 tokens
   const void *q;
   const float *km;
   const float *vm;
@@ -86,47 +103,49 @@ struct alignas(64) Params : ParamsHead {
 
 constexpr int kMaxCph = 256;  // CTAs per (sequence, KV head), bounded by the merge scratch
 
+constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
 template <int BITS, int D, int NT>
 struct Cfg {
-  static constexpr int KSTEPS = D / 16;
-  static constexpr int QT = BITS == 8 ? 32 : 64;        // tokens per K slot
-  static constexpr int QPB = 128 / QT;                  // K slots per block
-  static constexpr int TPL = QT / 8;                    // tokens per lane in a K slot
-  static constexpr int MTQ = QT / 16;                   // m-tiles per K slot
-  static constexpr int VSQ = QT / 32;                   // V slots per K slot
-  static constexpr int SPB = QPB * (1 + VSQ);           // slots per packed block
-  static constexpr int KSLOT = D * 32;                  // K slot bytes (TMA box 32 B x D)
-  static constexpr int KMETA = D * 8;                   // key (scale, low) of one block
-  static constexpr int VROWB = D * BITS / 8;            // bytes of one token's value codes
-  static constexpr int VBOX = VROWB < 128 ? VROWB : 128; // TMA box width (bytes)
-  static constexpr int NVB = VROWB / VBOX;              // boxes per value slot
+  static constexpr int ROWS = 8 * NT;                   // query rows incl. padding
+  // K stage: codes [D][SB] (one row per channel, 128 tokens) then (scale, low)[D].
+  static constexpr int SB = 128 * BITS / 8;
+  static constexpr int KCODE = D * SB;
+  static constexpr int KMETA = D * 8;
+  // Residual chunk: RCHUNK rows of D 16-bit values, padded pitch.
+  static constexpr int RP = 2 * D + 16;
+  static constexpr int RBYTES = RCHUNK * RP;
+  static constexpr int KST = align1k(cmax(KCODE + KMETA, RBYTES));
+  // V stage: codes [128][VROWB] in NVB boxes of VBOX bytes, then (scale, low)[128][NG].
+  static constexpr int VROWB = D * BITS / 8;
+  static constexpr int VBOX = VROWB < 128 ? VROWB : 128;
+  static constexpr int NVB = VROWB / VBOX;
   static constexpr int VSWZ = VBOX == 128 ? 7 : (VBOX == 64 ? 3 : 1);  // swizzle row mask
+  static constexpr int KSWZ = SB == 128 ? 7 : 3;
   static constexpr int NG = D / 64;
-  static constexpr int VMETA = 32 * NG * 8;             // value (scale, low) of 32 tokens
-  static constexpr int VSLOT = 32 * VROWB + VMETA;
-  // Value lane mapping: lane r owns CPL channels in each of NCH chunks.
-  static constexpr int CPL = BITS == 8 ? (D >= 128 ? 16 : 8) : D / 8;
-  static constexpr int NCH = D / (8 * CPL);
-  static constexpr int MTC = CPL / 2;                   // m-tiles per chunk
-  static constexpr int MTV = D / 16;                    // m-tiles of the output
-  // Residual slots (16 tokens of 16-bit values, padded pitch, cp.async).
-  static constexpr int RKP = 2 * D + 32;
-  static constexpr int RVP = CPL == 8 ? 2 * D + 32 : 2 * D + 16;
-  static constexpr int RSLOT_K = 16 * RKP;
-  static constexpr int RSLOT_V = 16 * RVP;
-  static constexpr int SLOT_RAW = KSLOT > VSLOT ? KSLOT : VSLOT;
-  static constexpr int SLOT_R = RSLOT_K > RSLOT_V ? RSLOT_K : RSLOT_V;
-  // Slots start on 1024-byte boundaries (required by the 128-byte swizzle).
-  static constexpr int SLOT = ((SLOT_RAW > SLOT_R ? SLOT_RAW : SLOT_R) + 1023) / 1024 * 1024;
-  static constexpr int PBUF = 8 * NT * PPITCH;
-  static constexpr int WARP_BYTES = (2 * SLOT + KMETA + PBUF + 1023) / 1024 * 1024;
-  static constexpr int QFRAG = KSTEPS * NT * 32 * 8;    // one fragment set
-  static constexpr int QFRAG_AL = (2 * QFRAG + 1023) / 1024 * 1024;
-  static constexpr int SMEM = 1024 + QFRAG_AL + WARPS * WARP_BYTES;  // + alignment slack
-  static constexpr int MERGE = WARPS * 8 * NT * (D + 2) * 4;
-  static_assert(MERGE <= WARPS * WARP_BYTES, "merge scratch must fit the warp region");
-  static_assert(2 * 16 * 256 * 4 + 16 * 2 * 4 <= WARPS * WARP_BYTES,
-                "final-merge scratch (rows x CTAs per pair) must fit the warp region");
+  static constexpr int VCODE = 128 * VROWB;
+  static constexpr int VMETA = 128 * NG * 8;
+  static constexpr int VST = align1k(cmax(VCODE + VMETA, RBYTES));
+  static constexpr int NV = NT == 1 ? 3 : 2;            // V stage ring depth
+  // QK: each warp covers all D channels in KQS k-steps of 16.
+  static constexpr int KQS = D / 16;
+  // PV: each warp covers D/4 channels, CPL per lane, MTV m-tiles.
+  static constexpr int CPL = D / 32;
+  static constexpr int MTV = CPL / 2;
+  // Shared-memory map (offsets from a 1024-byte aligned base).
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + NK * KST;
+  static constexpr int OFF_Q = OFF_V + NV * VST;                   // [KQS][NT][32] query B fragments
+  static constexpr int OFF_P = OFF_Q + KQS * NT * 32 * 8;          // [TEAMS][2][ROWS][PP]
+  static constexpr int OFF_XM = OFF_P + TEAMS * 2 * ROWS * PP;     // [TEAMS][2][4][ROWS] P scales m_q
+  static constexpr int OFF_END = OFF_XM + TEAMS * 2 * TEAM_WARPS * ROWS * 4;
+  static constexpr int SMEM = OFF_END + 1024;                      // + alignment slack
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  // End-of-CTA scratch (reuses the stage rings).
+  static constexpr int RED = TEAMS * ROWS * D * 4;                 // [team][ROWS][D]
+  static_assert(RED + 64 * ROWS * 4 <= NK * KST + NV * VST, "reduction scratch");
+  static_assert(16 * kMaxCph * 2 * 4 + 16 * 2 * 4 <= NK * KST + NV * VST, "merge scratch");
 };
 
 // Offset of byte `a` of a TMA box (rows of 128/64/32 bytes) after the hardware
@@ -137,161 +156,110 @@ __device__ __forceinline__ uint32_t swz(uint32_t a) {
   return a ^ (((a >> 7) & MASK) << 4);
 }
 
-// Residual PV token order: k-index (qd, e) -> token A[qd] + B[e].
-template <int CPL>
-__device__ __forceinline__ int resid_token(int qd, int e) {
-  if constexpr (CPL == 16) {
-    return ((qd & 1) | ((qd & 2) << 1)) + (((e & 1) << 1) | ((e & 2) << 2));
-  } else {
-    return qd + 4 * e;
-  }
-}
-// Position of residual token t in the permuted P row.
-template <int CPL>
-__device__ __forceinline__ int resid_pos(int t) {
-  if constexpr (CPL == 16) {
-    int qd = (t & 1) | ((t >> 1) & 2);
-    int e = ((t >> 1) & 1) | ((t >> 2) & 2);
-    return 4 * qd + e;
-  } else {
-    return 4 * (t & 3) + (t >> 2);
-  }
-}
-// Position of packed token t (0..63) in the permuted P row: within each
-// 16-token k-step, lane qd's four tokens 2qd, 2qd+1, 2qd+8, 2qd+9 sit at
-// 4qd..4qd+3 so its B fragment is one 8-byte load.
-__device__ __forceinline__ int packed_pos(int t) {
+// Position of token t of an item in a P row: within each 16-token k-step,
+// lane qd's four tokens 2qd, 2qd+1, 2qd+8, 2qd+9 sit at 4qd..4qd+3 so a PV
+// lane reads its B fragment with one 8-byte load.
+__device__ __forceinline__ int ppos(int t) {
   return (t & ~15) | (((t & 7) >> 1) << 2) | (((t >> 3) & 1) << 1) | (t & 1);
 }
 
+template <class T>
+__device__ __forceinline__ T lds(const uint8_t *base, uint32_t off) {
+  return *reinterpret_cast<const T *>(base + off);
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// 2^d for an integer-valued d <= 0; 0 below the normal range and for -inf
+// or NaN (the difference of two -inf scales).
+__device__ __forceinline__ float pow2i(float d) {
+  return !(d >= -126.f) ? 0.f : __int_as_float((int(d) + 127) << 23);
+}
+
+// Two codes held as 2^23 + code -> fma(code, scale, low) in fp32.
+__device__ __forceinline__ float2 dq2(float2 magic, float sc, float lo) {
+  const float2 c = __fadd2_rn(magic, make_float2(-kMagic, -kMagic));
+  return make_float2(__fmaf_rn(c.x, sc, lo), __fmaf_rn(c.y, sc, lo));
+}
+
+// The swizzle's XOR term for a row r of a 1024-byte swizzle atom depends only
+// on r's low bits (r & 7 for 128-byte rows, (r >> 1) & 3 for 64-byte rows,
+// (r >> 2) & 1 for 32-byte rows).  Rows that differ by a multiple of 8 share
+// it, so a lane computes its swizzled column once per row residue and adds
+// row * pitch for every other row.
+template <int MASK, int PITCH>
+__device__ __forceinline__ uint32_t swz_col(int row_rep, int col) {
+  return swz<MASK>(row_rep * PITCH + col) - row_rep * PITCH;
+}
+
+// ---------------------------------------------------------------------------
+// QK warp: partial logits of one item over half of the channels.
+// ---------------------------------------------------------------------------
 template <int BITS, int D, int NT, int DT>
-struct Warp {
+struct QkWarp {
   using C = Cfg<BITS, D, NT>;
   using E = Elem<DT>;
-  using T = typename E::T;
+  int lane, r, qd, q;
+  const uint8_t *qfr;   // query B fragments [KQS][NT][32] (shared memory)
 
-  // Per-lane state.
-  float acc[C::MTV][NT][4];
-  float m[NT][2], l[NT][2];
-  float S[C::MTQ][NT][4];
-
-  int lane, r, qd;
-  uint32_t qfp, qfr;          // fragment sets (shared addresses)
-  uint32_t ring, kmeta, pbuf; // per-warp shared regions
-  float scale_log2;
-
-  __device__ void init(int lane_, uint32_t qfp_, uint32_t qfr_, uint32_t base, float sl) {
-    lane = lane_;
-    r = lane >> 2;
-    qd = lane & 3;
-    qfp = qfp_;
-    qfr = qfr_;
-    ring = base;
-    kmeta = base + 2 * C::SLOT;
-    pbuf = kmeta + C::KMETA;
-    scale_log2 = sl;
-#pragma unroll
-    for (int i = 0; i < C::MTV; ++i)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        m[nt][j] = -INFINITY;
-        l[nt][j] = 0.f;
-      }
+  __device__ __forceinline__ uint2 qfrag(int s, int nt) const {
+    return lds<uint2>(qfr, ((s * NT + nt) * 32 + lane) * 8);
   }
 
-  // ---------------------------------------------------------------------
-  // Packed slot loads: lane 0 issues TMA tile copies (+ 1-D bulk copies of
-  // the metadata) that complete on the slot's mbarrier.
-  // ---------------------------------------------------------------------
-  __device__ void load_packed_k(const SeqDev &sd, int head, int unit, int quarter, uint32_t slot,
-                                bool with_meta, uint32_t bar) {
-    if (lane == 0) {
-      mbar_expect_tx(bar, C::KSLOT + (with_meta ? C::KMETA : 0));
-      tma_load_4d(slot, &sd.tk, bar, quarter * 32, 0, unit, head);
-      if (with_meta)
-        bulk_load(kmeta, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, bar);
-    }
-  }
-
-  __device__ void load_packed_v(const SeqDev &sd, int head, int tok0, uint32_t slot, uint32_t bar) {
-    if (lane == 0) {
-      mbar_expect_tx(bar, C::VSLOT);
+  // S[mt][nt][c]: tokens 32q + 4r + 2mt (c = 0, 1) and 32q + 4r + 2mt + 1
+  // (c = 2, 3), query rows 8nt + 2qd + (c & 1).
+  __device__ void packed(const uint8_t *kst, float (&S)[2][NT][4]) const {
 #pragma unroll
-      for (int bx = 0; bx < C::NVB; ++bx)
-        tma_load_3d(slot + bx * 32 * C::VBOX, &sd.tv, bar, bx * C::VBOX, tok0, head);
-      bulk_load(slot + 32 * C::VROWB, sd.vm + head * sd.vm_h + int64_t(tok0) * sd.vm_t, C::VMETA, bar);
-    }
-  }
-
-  // 16 residual tokens starting at window index t0 (rows >= re are zeroed).
-  __device__ void load_resid(const void *base_, int64_t stride_t, int t0, int re, uint32_t slot,
-                             int pitch) {
-    const T *base = static_cast<const T *>(base_);
-    constexpr int CH = D / 8;  // 16-byte chunks per row
-#pragma unroll 4
-    for (int x = lane; x < 16 * CH; x += 32) {
-      const int t = x / CH, k = x % CH;
-      const bool ok = t0 + t < re;
-      const T *src = base + (ok ? int64_t(t0 + t) * stride_t : 0) + k * 8;
-      cp_async16(slot + t * pitch + k * 16, src, ok ? 16 : 0);
-    }
-  }
-
-  // ---------------------------------------------------------------------
-  // QK^T over a packed K slot -> S (MTQ m-tiles of tokens x NT n-tiles)
-  // ---------------------------------------------------------------------
-  __device__ void qk_packed(uint32_t slot) {
-#pragma unroll
-    for (int mt = 0; mt < C::MTQ; ++mt)
+    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int c = 0; c < 4; ++c) S[mt][nt][c] = 0.f;
-#pragma unroll 2
-    for (int s = 0; s < C::KSTEPS; ++s) {
-      float f[4][C::TPL];  // [channel e][token within lane]
+    const uint8_t *meta = kst + C::KCODE;
+    // Channel rows 2qd + e_lo + 8 e_hi + 16 s share the swizzle term of
+    // 2qd + e_lo.
+    const int col = BITS == 8 ? 32 * q + 4 * r : 16 * q + 2 * r;
+    const uint8_t *krow[2];
+#pragma unroll
+    for (int el = 0; el < 2; ++el)
+      krow[el] = kst + (2 * qd + el) * C::SB + swz_col<C::KSWZ, C::SB>(2 * qd + el, col);
+#pragma unroll 4
+    for (int s = 0; s < C::KQS; ++s) {
+      const int cb = 16 * s + 2 * qd;   // channels cb, cb+1, cb+8, cb+9
+      const float4 m0 = lds<float4>(meta, cb * 8);
+      const float4 m1 = lds<float4>(meta, (cb + 8) * 8);
+      const float sc[4] = {m0.x, m0.z, m1.x, m1.z};
+      const float lo[4] = {m0.y, m0.w, m1.y, m1.w};
+      float f[4][4];  // [channel e][token j]
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int c = 16 * s + qd + 4 * e;
-        const uint32_t w = lds32(slot + c * 32 + 4 * r);
-        const float2 sm = lds64f(kmeta + c * 8);
-        const float2 sc = make_float2(sm.x, sm.x), lo = make_float2(sm.y, sm.y);
+        const uint8_t *src = krow[e & 1] + (16 * s + 8 * (e >> 1)) * C::SB;
+        float2 x0, x1;
         if constexpr (BITS == 8) {
-          float2 x0 = make_float2(byte_magic<0>(w), byte_magic<1>(w));
-          float2 x1 = make_float2(byte_magic<2>(w), byte_magic<3>(w));
-          x0 = __fadd2_rn(x0, make_float2(-kMagic, -kMagic));
-          x1 = __fadd2_rn(x1, make_float2(-kMagic, -kMagic));
-          x0 = __ffma2_rn(x0, sc, lo);
-          x1 = __ffma2_rn(x1, sc, lo);
-          f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
+          const uint32_t w = *reinterpret_cast<const uint32_t *>(src);
+          x0 = make_float2(byte_magic<0>(w), byte_magic<1>(w));
+          x1 = make_float2(byte_magic<2>(w), byte_magic<3>(w));
         } else {
-          // byte b holds tokens 2b (low nibble) and 2b+1 (high nibble)
-          const uint32_t lo4 = w & 0x0F0F0F0Fu, hi4 = (w >> 4) & 0x0F0F0F0Fu;
-          float2 x0 = make_float2(byte_magic<0>(lo4), byte_magic<0>(hi4));
-          float2 x1 = make_float2(byte_magic<1>(lo4), byte_magic<1>(hi4));
-          float2 x2 = make_float2(byte_magic<2>(lo4), byte_magic<2>(hi4));
-          float2 x3 = make_float2(byte_magic<3>(lo4), byte_magic<3>(hi4));
-          const float2 mg = make_float2(-kMagic, -kMagic);
-          x0 = __ffma2_rn(__fadd2_rn(x0, mg), sc, lo);
-          x1 = __ffma2_rn(__fadd2_rn(x1, mg), sc, lo);
-          x2 = __ffma2_rn(__fadd2_rn(x2, mg), sc, lo);
-          x3 = __ffma2_rn(__fadd2_rn(x3, mg), sc, lo);
-          f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
-          f[e][4] = x2.x; f[e][5] = x2.y; f[e][6] = x3.x; f[e][7] = x3.y;
+          // two bytes: tokens 4r+0 (low nibble), +1 (high), +2, +3
+          const uint32_t w = *reinterpret_cast<const uint16_t *>(src);
+          const uint32_t lo4 = w & 0x0F0Fu, hi4 = (w >> 4) & 0x0F0Fu;
+          x0 = make_float2(byte_magic<0>(lo4), byte_magic<0>(hi4));
+          x1 = make_float2(byte_magic<1>(lo4), byte_magic<1>(hi4));
         }
+        x0 = dq2(x0, sc[e], lo[e]);
+        x1 = dq2(x1, sc[e], lo[e]);
+        f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
       }
       uint2 b[NT];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(qfp + ((s * NT + nt) * 32 + lane) * 8);
+      for (int nt = 0; nt < NT; ++nt) b[nt] = qfrag(s, nt);
 #pragma unroll
-      for (int mt = 0; mt < C::MTQ; ++mt) {
-        // m-tile mt: row r <-> lane token 2mt, row r+8 <-> lane token 2mt+1
+      for (int mt = 0; mt < 2; ++mt) {
         uint32_t a[4];
         a[0] = E::pack2(f[0][2 * mt], f[1][2 * mt]);
         a[1] = E::pack2(f[0][2 * mt + 1], f[1][2 * mt + 1]);
@@ -303,200 +271,160 @@ struct Warp {
     }
   }
 
-  // QK^T over a residual K slot (16 tokens, one m-tile) -> S[0]
-  __device__ void qk_resid(uint32_t slot) {
+  // Residual chunk: one m-tile of tokens 16q + r (c = 0, 1) and 16q + r + 8
+  // (c = 2, 3).
+  __device__ void resid(uint32_t kst, float (&S)[NT][4]) const {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) S[0][nt][c] = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < C::KSTEPS; ++s) {
-      const uint2 w0 = lds64(slot + r * C::RKP + (16 * s + 4 * qd) * 2);
-      const uint2 w1 = lds64(slot + (r + 8) * C::RKP + (16 * s + 4 * qd) * 2);
-      uint32_t a[4] = {w0.x, w1.x, w0.y, w1.y};
+      for (int c = 0; c < 4; ++c) S[nt][c] = 0.f;
+    const int row = 16 * q + (lane & 7) + 8 * ((lane >> 3) & 1);
+    const uint32_t base = kst + row * C::RP + 8 * (lane >> 4) * 2;
+#pragma unroll
+    for (int s = 0; s < C::KQS; ++s) {
+      uint32_t a[4];
+      ldmatrix_x4(a, base + 32 * s);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint2 b = lds64(qfr + ((s * NT + nt) * 32 + lane) * 8);
-        mma16816<DT>(S[0][nt], a, b.x, b.y);
+        const uint2 b = qfrag(s, nt);
+        mma16816<DT>(S[nt], a, b.x, b.y);
       }
     }
   }
+};
 
-  // ---------------------------------------------------------------------
-  // Online softmax over the S tile; writes permuted P; rescales acc.
-  //   MT       m-tiles in S
-  //   tok(m,h) token (slot-local) of row r (h=0) / r+8 (h=1) of m-tile m
-  //   valid(t, row) mask (true for packed tokens)
-  //   pos(t)   column of token t in the permuted P row
-  // ---------------------------------------------------------------------
-  template <int MT, class Tok, class Valid, class Pos>
-  __device__ void softmax(Tok tok, Valid valid, Pos pos) {
-    float alpha[NT][2];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int row = 8 * nt + 2 * qd + j;
-        float v[2 * MT];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float x = S[mt][nt][2 * h + j] * scale_log2;
-            if (!valid(tok(mt, h), row)) x = -INFINITY;
-            v[2 * mt + h] = x;
-            mx = fmaxf(mx, x);
-          }
-        }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-        const float mnew = fmaxf(m[nt][j], mx);
-        const float muse = mnew == -INFINITY ? 0.f : mnew;
-        alpha[nt][j] = ex2(m[nt][j] - muse);
-        m[nt][j] = mnew;
-        float sum = 0.f;
-        const uint32_t prow = pbuf + row * PPITCH;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float p = ex2(v[2 * mt + h] - muse);
-            sum += p;
-            const T ph = E::from_f32(p);
-            const uint16_t bits = *reinterpret_cast<const uint16_t *>(&ph);
-            asm volatile("st.shared.u16 [%0], %1;" ::"r"(prow + pos(tok(mt, h)) * 2), "h"(bits));
-          }
-        }
-        l[nt][j] = l[nt][j] * alpha[nt][j] + sum;
-      }
-    }
-    bool unit = true;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) unit = unit && alpha[nt][0] == 1.f && alpha[nt][1] == 1.f;
-    if (!__all_sync(0xffffffffu, unit)) {
-#pragma unroll
-      for (int i = 0; i < C::MTV; ++i)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float2 al = make_float2(alpha[nt][0], alpha[nt][1]);
-          float2 x0 = __fmul2_rn(make_float2(acc[i][nt][0], acc[i][nt][1]), al);
-          float2 x1 = __fmul2_rn(make_float2(acc[i][nt][2], acc[i][nt][3]), al);
-          acc[i][nt][0] = x0.x; acc[i][nt][1] = x0.y;
-          acc[i][nt][2] = x1.x; acc[i][nt][3] = x1.y;
-        }
-    }
-  }
+// ---------------------------------------------------------------------------
+// PV warp: O += P.V over one item's token half and channel quarter.
+// O[i][nt][c]: channel (D/4)c + CPL r + 2i + (c >> 1), query row 8nt + 2qd + (c & 1).
+// ---------------------------------------------------------------------------
+template <int BITS, int D, int NT, int DT>
+struct PvWarp {
+  using C = Cfg<BITS, D, NT>;
+  using E = Elem<DT>;
+  int lane, r, qd, c;
 
-  // ---------------------------------------------------------------------
-  // P.V over a packed V slot of 32 tokens; kbase = first PV k-step of the
-  // slot within the current K slot's P row.
-  // ---------------------------------------------------------------------
-  __device__ void pv_packed(uint32_t slot, int kbase) {
-    const uint32_t meta = slot + 32 * C::VROWB;
+  // fb[q][nt]: packed factor pair for the P fragments written by QK warp q
+  // (applied when `scaled`).
+  __device__ void packed(const uint8_t *vst, const uint8_t *pb, float (&O)[C::MTV][NT][4],
+                         const uint32_t (&fb)[TEAM_WARPS][NT], bool scaled) const {
+    constexpr int CB = C::CPL * BITS / 8;            // code bytes per lane per token
+    const int off = ((D / 4) * c + C::CPL * r) * BITS / 8;   // lane's first byte in a row
+    const uint8_t *box = vst + (off / C::VBOX) * 128 * C::VBOX;
+    const int inb = off % C::VBOX;
+    const int grp = ((D / 4) * c) / 64;
+    // Token rows t = t0 + e_lo + 8 e_hi + 16 j with t0 = 2 qd share the
+    // swizzle term of 2 qd + e_lo.
+    const int t0 = 2 * qd;
+    const uint8_t *vrow[2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int el = 0; el < 2; ++el)
+      vrow[el] = box + (t0 + el) * C::VBOX + swz_col<C::VSWZ, C::VBOX>(2 * qd + el, inb);
+    const uint8_t *meta = vst + C::VCODE + (t0 * C::NG + grp) * 8;
+    const uint8_t *prow = pb + r * PP + 4 * qd * 2;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
       uint2 b[NT];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        b[nt] = lds64(pbuf + (8 * nt + r) * PPITCH + (16 * (kbase + j) + 4 * qd) * 2);
+      for (int nt = 0; nt < NT; ++nt) {
+        b[nt] = lds<uint2>(prow, 8 * nt * PP + 32 * j);
+        if (scaled) {
+          b[nt].x = E::mul2(b[nt].x, fb[j >> 1][nt]);
+          b[nt].y = E::mul2(b[nt].y, fb[j >> 1][nt]);
+        }
+      }
+      uint32_t w[4][CB >= 4 ? CB / 4 : 1];
+      float sc[4], lo[4];
 #pragma unroll
-      for (int ch = 0; ch < C::NCH; ++ch) {
-        const int c0 = ch * 8 * C::CPL + C::CPL * r;   // lane's first channel in chunk
-        const int grp = c0 / 64;
-        constexpr int CB = C::CPL * BITS / 8;           // code bytes per token per chunk
-        uint32_t w[4][CB / 4 > 0 ? CB / 4 : 1];
-        float2 sc[4], lo[4];
+      for (int e = 0; e < 4; ++e) {
+        const int dt = 16 * j + 8 * (e >> 1);       // token offset beyond t0 + e_lo
+        const uint8_t *src = vrow[e & 1] + dt * C::VBOX;
+        if constexpr (CB == 8) {
+          const uint2 v = *reinterpret_cast<const uint2 *>(src);
+          w[e][0] = v.x; w[e][1] = v.y;
+        } else if constexpr (CB == 4) {
+          w[e][0] = *reinterpret_cast<const uint32_t *>(src);
+        } else if constexpr (CB == 2) {
+          w[e][0] = *reinterpret_cast<const uint16_t *>(src);
+        } else {
+          w[e][0] = *src;
+        }
+        const float2 sm = lds<float2>(meta, ((dt + (e & 1)) * C::NG) * 8);
+        sc[e] = sm.x;
+        lo[e] = sm.y;
+      }
+#pragma unroll
+      for (int i = 0; i < C::MTV; ++i) {
+        // channels CPL r + 2i (row r) and CPL r + 2i + 1 (row r + 8)
+        float2 x[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          // k-index 2qd, 2qd+1, 2qd+8, 2qd+9 <-> slot token 16j + the same
-          const int t = 16 * j + 2 * qd + (e & 1) + 8 * (e >> 1);
-          const int off = c0 * BITS / 8;                 // byte of the lane's chunk in the row
-          const uint32_t addr = slot + (off / C::VBOX) * 32 * C::VBOX +
-                                swz<C::VSWZ>(t * C::VBOX + off % C::VBOX);
-          if constexpr (CB == 16) {
-            uint4 v = lds128(addr);
-            w[e][0] = v.x; w[e][1] = v.y; w[e][2] = v.z; w[e][3] = v.w;
-          } else if constexpr (CB == 8) {
-            uint2 v = lds64(addr);
-            w[e][0] = v.x; w[e][1] = v.y;
+          if constexpr (BITS == 8) {
+            const uint32_t word = w[e][i >> 1];
+            x[e] = (i & 1) ? make_float2(byte_magic<2>(word), byte_magic<3>(word))
+                           : make_float2(byte_magic<0>(word), byte_magic<1>(word));
           } else {
-            w[e][0] = lds32(addr);
+            // byte i holds channel 2i (low nibble) and 2i + 1 (high nibble)
+            const uint32_t word = w[e][i >> 2];
+            const uint32_t lo4 = word & 0x0F0F0F0Fu, hi4 = (word >> 4) & 0x0F0F0F0Fu;
+            const uint32_t sel = 0x7440u | (i & 3);
+            x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
+                               __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
           }
-          const float2 sm = lds64f(meta + (t * C::NG + grp) * 8);
-          sc[e] = make_float2(sm.x, sm.x);
-          lo[e] = make_float2(sm.y, sm.y);
+          x[e] = dq2(x[e], sc[e], lo[e]);
         }
+        uint32_t a[4];
+        a[0] = E::pack2(x[0].x, x[1].x);
+        a[1] = E::pack2(x[0].y, x[1].y);
+        a[2] = E::pack2(x[2].x, x[3].x);
+        a[3] = E::pack2(x[2].y, x[3].y);
 #pragma unroll
-        for (int i = 0; i < C::MTC; ++i) {
-          // channels c0 + 2i (row r) and c0 + 2i + 1 (row r+8)
-          float2 x[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if constexpr (BITS == 8) {
-              const uint32_t word = w[e][i >> 1];
-              x[e] = (i & 1) ? make_float2(byte_magic<2>(word), byte_magic<3>(word))
-                             : make_float2(byte_magic<0>(word), byte_magic<1>(word));
-            } else {
-              const uint32_t word = w[e][i >> 2];
-              const uint32_t lo4 = word & 0x0F0F0F0Fu, hi4 = (word >> 4) & 0x0F0F0F0Fu;
-              const int bsel = i & 3;
-              const uint32_t sel = 0x7440u | bsel;
-              x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
-                                 __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
-            }
-            x[e] = __ffma2_rn(__fadd2_rn(x[e], make_float2(-kMagic, -kMagic)), sc[e], lo[e]);
-          }
-          uint32_t a[4];
-          a[0] = E::pack2(x[0].x, x[1].x);
-          a[1] = E::pack2(x[0].y, x[1].y);
-          a[2] = E::pack2(x[2].x, x[3].x);
-          a[3] = E::pack2(x[2].y, x[3].y);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            mma16816<DT>(acc[ch * C::MTC + i][nt], a, b[nt].x, b[nt].y);
-        }
+        for (int nt = 0; nt < NT; ++nt) mma16816<DT>(O[i][nt], a, b[nt].x, b[nt].y);
       }
     }
   }
 
-  // P.V over a residual V slot (16 tokens, exact values).
-  __device__ void pv_resid(uint32_t slot) {
-    uint2 b[NT];
+  // Residual chunk: exact 16-bit values, tokens 16j + {2qd, 2qd+1, 2qd+8, 2qd+9}.
+  __device__ void resid(const uint8_t *vst, const uint8_t *pb, float (&O)[C::MTV][NT][4],
+                        const uint32_t (&fb)[TEAM_WARPS][NT], bool scaled) const {
+    const uint32_t coff = ((D / 4) * c + C::CPL * r) * 2;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) b[nt] = lds64(pbuf + (8 * nt + r) * PPITCH + 4 * qd * 2);
+    for (int j = 0; j < RCHUNK / 16; ++j) {
+      const int t0 = 16 * j + 2 * qd;
+      uint2 b[NT];
 #pragma unroll
-    for (int ch = 0; ch < C::NCH; ++ch) {
-      const int c0 = ch * 8 * C::CPL + C::CPL * r;
-#pragma unroll
-      for (int piece = 0; piece < C::CPL / 8; ++piece) {
-        uint4 w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int t = resid_token<C::CPL>(qd, e);
-          w[e] = lds128(slot + t * C::RVP + (c0 + 8 * piece) * 2);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t w0 = (&w[0].x)[k], w1 = (&w[1].x)[k], w2 = (&w[2].x)[k],
-                         w3 = (&w[3].x)[k];
-          uint32_t a[4];
-          a[0] = prmt(w0, w1, 0x5410u);
-          a[1] = prmt(w0, w1, 0x7632u);
-          a[2] = prmt(w2, w3, 0x5410u);
-          a[3] = prmt(w2, w3, 0x7632u);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            mma16816<DT>(acc[ch * C::MTC + piece * 4 + k][nt], a, b[nt].x, b[nt].y);
+      for (int nt = 0; nt < NT; ++nt) {
+        b[nt] = lds<uint2>(pb, (8 * nt + r) * PP + (16 * j + 4 * qd) * 2);
+        if (scaled) {
+          b[nt].x = E::mul2(b[nt].x, fb[j][nt]);
+          b[nt].y = E::mul2(b[nt].y, fb[j][nt]);
         }
       }
+      uint32_t w[4][C::MTV];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = t0 + (e & 1) + 8 * (e >> 1);
+        const uint32_t a = t * C::RP + coff;
+        if constexpr (C::MTV == 4) {
+          const uint4 v = lds<uint4>(vst, a);
+          w[e][0] = v.x; w[e][1] = v.y; w[e][2] = v.z; w[e][3] = v.w;
+        } else if constexpr (C::MTV == 2) {
+          const uint2 v = lds<uint2>(vst, a);
+          w[e][0] = v.x; w[e][1] = v.y;
+        } else {
+          w[e][0] = lds<uint32_t>(vst, a);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < C::MTV; ++i) {
+        uint32_t a[4];
+        a[0] = prmt(w[0][i], w[1][i], 0x5410u);
+        a[1] = prmt(w[0][i], w[1][i], 0x7632u);
+        a[2] = prmt(w[2][i], w[3][i], 0x5410u);
+        a[3] = prmt(w[2][i], w[3][i], 0x7632u);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<DT>(O[i][nt], a, b[nt].x, b[nt].y);
+      }
     }
-  }
-
-  // Channel of acc[i][*][c] for this lane (c = 0,1 -> row r; 2,3 -> row r+8).
-  __device__ __forceinline__ int out_channel(int i, int c) const {
-    return (i / C::MTC) * 8 * C::CPL + C::CPL * r + 2 * (i % C::MTC) + (c >> 1);
   }
 };
 

@@ -36,6 +36,12 @@ template <> struct Elem<CKV_BF16> {
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
   }
+  // Elementwise product of two packed pairs.
+  __device__ static uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+  }
 };
 template <> struct Elem<CKV_F16> {
   using T = __half;
@@ -44,6 +50,11 @@ template <> struct Elem<CKV_F16> {
   __device__ static uint32_t pack2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  __device__ static uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
 };
@@ -104,18 +115,19 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
-// D = A * B + D, m16n8k16, fp32 accumulate.
+// D = A * B + D, m16n8k16, fp32 accumulate.  Not volatile: a pure function
+// of its registers, so the compiler may schedule it among the loads.
 template <int DT>
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
   if constexpr (DT == CKV_BF16) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
         "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
         "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -177,6 +189,11 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void *tmap, uint
       "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
       : "memory");
+}
+// The mbarrier's current phase also waits for this thread's earlier cp.async
+// copies (pending count +1 now, -1 when they land: net zero).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 // Contiguous global -> shared bulk copy (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
