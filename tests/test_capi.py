@@ -55,7 +55,8 @@ def test_attention_rejects_null_and_oversized_requests():
 def test_torch_ops_register_without_cuda():
     _native.load()
     import torch
-    for op in ('pack_rows', 'unpack_rows', 'pack_append', 'attention', 'combine_partials'):
+    for op in ('pack_rows', 'unpack_rows', 'pack_append', 'attention', 'combine_partials', 'decode',
+               'attention_error'):
         assert hasattr(torch.ops.ckv, op)
 
 

@@ -189,3 +189,32 @@ def test_decode_does_not_modify_the_view_and_reuses_across_lengths():
             assert run(q, v, .125) is not None
             layer.compact_residual()
     assert layer.get_seq_length() == 1325
+
+
+def test_long_decode_loop_never_gives_up_a_wait():
+    """Thousands of decode launches through append / decode / compact (the
+    bench's 32K-context step on 4 layers): no kernel may abort a wait.  An
+    abort means a pipeline barrier lost track of its phase (it used to
+    happen about once in 8000 launches when one team of warps ran a stage
+    ahead of the other), and that call's output would be wrong."""
+    from trpg_b200.compressed_kv_kernels import attention_error, decode
+    from trpg_b200.quantized_kv import QuantizedAttentionLayer
+    gen = torch.Generator(device='cuda').manual_seed(21)
+    attention_error()   # clear anything left by earlier tests
+    with torch.inference_mode():
+        layers = []
+        for _ in range(4):
+            k = torch.randn(1, 4, 32767, 256, generator=gen, device='cuda').bfloat16()
+            v = torch.randn(1, 4, 32767, 256, generator=gen, device='cuda').bfloat16()
+            layer = QuantizedAttentionLayer(8)
+            layer.update(k, v)
+            layers.append(layer)
+        q = torch.randn(64, 1, 16, 1, 256, generator=gen, device='cuda').bfloat16()
+        kn = torch.randn(64, 1, 4, 1, 256, generator=gen, device='cuda').bfloat16()
+        for step in range(2500):
+            for layer in layers:
+                view = layer.append_for_attention(kn[step % 64], kn[(step + 1) % 64])
+                decode(q[step % 64], view, 1 / 16)
+                layer.compact_residual()
+        torch.cuda.synchronize()
+    assert attention_error() == 0

@@ -117,6 +117,18 @@ def verify(query: torch.Tensor, view, scale: float) -> torch.Tensor:
     return _single(query, view, scale)
 
 
+def attention_error(device=None) -> int:
+    """1 if an attention call on ``device`` gave up waiting inside the kernel
+    (its outputs are then invalid) since the last check, else 0; clears it.
+
+    The kernels bound every wait (about a second) instead of hanging; this
+    reports such an event.  It waits for the device's streams that ran
+    attention calls.
+    """
+    dev = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+    return int(ops().attention_error(torch.empty(0, device=dev)))
+
+
 def combine(partials: Sequence[torch.Tensor] | torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """Log-sum-exp merge of split-KV partials (``compressed_kv_kernels.py:85-89``).
 

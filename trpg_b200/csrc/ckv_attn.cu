@@ -32,6 +32,24 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   return true;
 }
 
+// Wait until the producer has issued `item` into a ring stage (its index is
+// published in `slot`), then for that item's data.  A parity wait only tells
+// the current phase from the one before it, and the two teams use a ring
+// stage alternately, so a team can reach its item while the other team's
+// previous item of the stage is still in flight: waiting on the parity alone
+// would then match that older phase.  Once the item is known to be issued,
+// the stage's barrier is at most one phase behind it and the parity is exact.
+__device__ __forceinline__ bool wait_stage(uint32_t bar, volatile int *slot, int item, int ph,
+                                           volatile int *abort) {
+  if (*slot < item) {
+    const long long start = clock64();
+    while (*slot < item) {
+      if (*abort || clock64() - start > (1ll << 31)) return false;
+    }
+  }
+  return wait_or_abort(bar, ph & 1, abort);
+}
+
 template <int BITS, int D, int NT, int DT, int MAXS>
 __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant__ Params<MAXS> p) {
   using C = Cfg<BITS, D, NT>;
@@ -40,6 +58,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ int s_seq, s_last;
   __shared__ volatile int s_abort;
+  __shared__ volatile int s_issued[NK + NV];   // last item issued into each K, then V, stage
   // kfull[NK] kempty[NK] vfull[NV] vempty[NV] pfull[TEAMS][2] pempty[TEAMS][2]
   __shared__ __align__(8) uint64_t s_bar[2 * NK + 2 * NV + 4 * TEAMS];
   // 1024-byte aligned base: the TMA swizzle patterns repeat every 1024 bytes.
@@ -59,6 +78,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     }
     s_seq = lo;
     s_abort = 0;
+    for (int i = 0; i < NK + NV; ++i) s_issued[i] = -1;
     for (int i = 0; i < NK; ++i) {
       mbar_init(bar(KFULL + i), 1);
       mbar_init(bar(KEMPTY + i), TEAM_THREADS);
@@ -176,6 +196,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
         if (lane == 0) mbar_arrive(fb);
       }
       __syncwarp();
+      if (lane == 0) s_issued[(kchain ? 0 : NK) + st] = i;
       issued = i + 1;
     }
     // Let every issued copy land before the stage memory is reused.
@@ -207,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       const int it = ib + i;
       const bool pk = it < np;
       float S[2][NT][4];
-      const bool have = !s_abort && wait_or_abort(bar(KFULL + st), (i / NK) & 1, &s_abort);
+      const bool have = !s_abort && wait_stage(bar(KFULL + st), &s_issued[st], i, i / NK, &s_abort);
       if (!have && !s_abort) fail();
       if (have) {
         if (pk) qw.packed(smem + C::OFF_K + st * C::KST, S);
@@ -302,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       const int k = i >> 1, par = k & 1;
       const int sv = i % NV;
       const bool pk = ib + i < np;
-      bool ok = !s_abort && wait_or_abort(bar(VFULL + sv), (i / NV) & 1, &s_abort);
+      bool ok = !s_abort && wait_stage(bar(VFULL + sv), &s_issued[NK + sv], i, i / NV, &s_abort);
       ok = ok && wait_or_abort(bar(PFULL + team * 2 + par), (k >> 1) & 1, &s_abort);
       if (!ok && !s_abort) fail();
       if (ok) {
@@ -438,9 +459,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       recml[row * 2 + 1] = L[0] * w0 + L[1] * w1;
     }
   }
-  __threadfence();
   __syncthreads();
   if (tid == 0) {
+    __threadfence();   // the whole CTA's record stores (ordered by the barrier) before the ticket
     const unsigned prev = atomicAdd(&p.counters[seq * p.hkv + head], 1u);
     s_last = prev == unsigned(sd.cph - 1);
   }

@@ -186,6 +186,10 @@ __device__ __forceinline__ float2 dq2(float2 magic, float sc, float lo) {
   const float2 c = __fadd2_rn(magic, make_float2(-kMagic, -kMagic));
   return make_float2(__fmaf_rn(c.x, sc, lo), __fmaf_rn(c.y, sc, lo));
 }
+// The same with (scale, scale) and (low, low) already paired.
+__device__ __forceinline__ float2 dq2p(float2 magic, float2 sc, float2 lo) {
+  return __ffma2_rn(__fadd2_rn(magic, make_float2(-kMagic, -kMagic)), sc, lo);
+}
 
 // The swizzle's XOR term for a row r of a 1024-byte swizzle atom depends only
 // on r's low bits (r & 7 for 128-byte rows, (r >> 1) & 3 for 64-byte rows,
@@ -333,7 +337,7 @@ struct PvWarp {
         }
       }
       uint32_t w[4][CB >= 4 ? CB / 4 : 1];
-      float sc[4], lo[4];
+      float2 sc[4], lo[4];   // one token's (scale, low), paired for its CPL channels
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int dt = 16 * j + 8 * (e >> 1);       // token offset beyond t0 + e_lo
@@ -349,8 +353,8 @@ struct PvWarp {
           w[e][0] = *src;
         }
         const float2 sm = lds<float2>(meta, ((dt + (e & 1)) * C::NG) * 8);
-        sc[e] = sm.x;
-        lo[e] = sm.y;
+        sc[e] = make_float2(sm.x, sm.x);
+        lo[e] = make_float2(sm.y, sm.y);
       }
 #pragma unroll
       for (int i = 0; i < C::MTV; ++i) {
@@ -370,7 +374,7 @@ struct PvWarp {
             x[e] = make_float2(__uint_as_float(prmt(lo4, 0x4B000000u, sel)),
                                __uint_as_float(prmt(hi4, 0x4B000000u, sel)));
           }
-          x[e] = dq2(x[e], sc[e], lo[e]);
+          x[e] = dq2p(x[e], sc[e], lo[e]);
         }
         uint32_t a[4];
         a[0] = E::pack2(x[0].x, x[1].x);

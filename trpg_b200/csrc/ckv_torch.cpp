@@ -345,6 +345,31 @@ Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
   return out;
 }
 
+// Error word of every cached attention workspace on `like`'s device (1 when
+// a kernel gave up waiting for a copy or a peer warp and aborted, so that
+// call's outputs are not valid).  Reading waits for each stream; the words
+// are cleared afterwards.
+int64_t attention_error(const Tensor &like) {
+  TORCH_CHECK(like.is_cuda(), "ckv::attention_error: a CUDA tensor names the device");
+  const int dev = int(like.get_device());
+  auto &ws = workspaces();
+  std::lock_guard<std::mutex> lock(ws.mu);
+  int64_t any = 0;
+  for (auto &kv : ws.buffers) {
+    if (kv.first.first != dev) continue;
+    int flag = 0;
+    check_status(ckv_attention_error(kv.second.data_ptr(), &flag,
+                                     reinterpret_cast<ckv_stream_t>(kv.first.second)),
+                 "attention_error");
+    if (flag) {
+      C10_CUDA_CHECK(cudaMemsetAsync(kv.second.data_ptr(), 0, 4, kv.first.second));
+      C10_CUDA_CHECK(cudaStreamSynchronize(kv.first.second));
+      any = 1;
+    }
+  }
+  return any;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(ckv, m) {
@@ -362,6 +387,7 @@ TORCH_LIBRARY(ckv, m) {
   m.def(
       "decode(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
       "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
+  m.def("attention_error(Tensor like) -> int");
 }
 
 namespace {
@@ -396,4 +422,5 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("attention", &attention_opt);
   m.impl("combine_partials", &combine_partials);
   m.impl("decode", &decode);
+  m.impl("attention_error", &attention_error);
 }
