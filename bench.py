@@ -28,7 +28,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -85,50 +84,83 @@ def max_over_ranks(x: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 # Clocks sampled during the timed region
 # ---------------------------------------------------------------------------
+# A child process samples the SM clock and the clock-event reasons through
+# NVML (read-only queries) every 20 ms and writes one flushed line per sample:
+# "<unix time> <MHz> <max MHz> <reason mask>".
+_SAMPLER = r"""
+import sys, time, pynvml as nv
+nv.nvmlInit()
+uuid, out = sys.argv[1], sys.argv[2]
+handle = None
+for i in range(nv.nvmlDeviceGetCount()):
+    h = nv.nvmlDeviceGetHandleByIndex(i)
+    u = nv.nvmlDeviceGetUUID(h)
+    u = u.decode() if isinstance(u, bytes) else u
+    if u.replace('GPU-', '') == uuid:
+        handle = h
+if handle is None:
+    handle = nv.nvmlDeviceGetHandleByIndex(0)
+mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+with open(out, 'w') as f:
+    while True:
+        mhz = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
+        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+        f.write(f'{time.time()} {mhz} {mx} {mask}\n')
+        f.flush()
+        time.sleep(0.02)
+"""
+
+
 class Clocks:
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
-              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
-              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+    """SM clock and clock-event reasons during a time window, sampled by a
+    child process so that the benchmark's own launches are not slowed."""
+    REASONS = (('hw_slowdown', 0x8), ('sw_power_cap', 0x4), ('hw_thermal_slowdown', 0x40),
+               ('sw_thermal_slowdown', 0x20), ('hw_power_brake', 0x80))
 
     def __init__(self, device: int):
-        self.device, self.proc = device, None
+        import subprocess
+        import tempfile
+        self.path = tempfile.mktemp(prefix='bench_clocks_', suffix='.txt')
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.proc = subprocess.Popen([sys.executable, '-c', _SAMPLER, uuid, self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, RuntimeError, AttributeError):
+            self.proc = None
+        self.t0 = self.t1 = None
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                 '-lms', '20', '-i', str(self.device)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, ValueError):
-            self.proc = None
+        self.t0 = time.time()
 
     def stop(self):
+        self.t1 = time.time()
+
+    def summary(self):
         if self.proc is None:
             return {'samples': 0}
+        time.sleep(0.05)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
-        except subprocess.TimeoutExpired:
+            self.proc.wait(timeout=10)
+        except Exception:
             self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], 0.0, set()
-        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
-        for line in out.strip().splitlines():
-            parts = [p.strip() for p in line.split(',')]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == 'active':
-                    reasons.add(name)
-        if not sm:
-            return {'samples': 0}
-        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons),
-                'samples': len(sm)}
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = line.split()
+                    if len(parts) == 4:
+                        rows.append((float(parts[0]), float(parts[1]), float(parts[2]), int(parts[3])))
+            os.unlink(self.path)
+        except OSError:
+            pass
+        inside = [r for r in rows if self.t0 is not None and self.t0 <= r[0] <= self.t1]
+        if not inside:
+            return {'samples': 0, 'samples_total': len(rows)}
+        reasons = sorted({name for _, _, _, mask in inside for name, bit in self.REASONS if mask & bit})
+        return {'sm_mhz': statistics.median(r[1] for r in inside), 'sm_max_mhz': max(r[2] for r in inside),
+                'reasons': reasons, 'samples': len(inside)}
 
 
 # ---------------------------------------------------------------------------
@@ -306,6 +338,7 @@ def b200_arm(args, world, rank, local):
     _native.load()
     device = torch.device('cuda', local)
     torch.cuda.set_device(device)
+    clocks = Clocks(local)          # the sampler starts while the caches are built
     seq = Sequence(1000 + rank, args.steps + args.warmup, device)
     # untimed warm-up
     run_steps(seq, decode, args.warmup)
@@ -313,7 +346,6 @@ def b200_arm(args, world, rank, local):
     torch.cuda.synchronize()
 
     # ---- device-timed region ------------------------------------------------
-    clocks = Clocks(local)
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
@@ -324,7 +356,7 @@ def b200_arm(args, world, rank, local):
     stop.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
-    clk = clocks.stop()
+    clocks.stop()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(stop), world)
     seq.rollback()
@@ -379,7 +411,7 @@ def b200_arm(args, world, rank, local):
                          'kernel': 'attn_kernel<8,256,1,bf16>',
                          'bytes_per_launch': bytes_per_launch, 'us_per_launch': sec * 1e6},
             'hbm_gbs_step': world * LAYERS * bytes_per_launch * args.steps / (ms * 1e-3) / 1e9 / world,
-            'clocks': clk,
+            'clocks': clocks.summary(),
             'e2e': {'value': world * e2e_steps / (e2e_ms * 1e-3), 'unit': 'tok/s',
                     'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
                     'us_per_step': e2e_ms * 1e3 / e2e_steps},
