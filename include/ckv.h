@@ -99,6 +99,26 @@ typedef struct {
 
 int ckv_pack_append(const ckv_append_args *args, ckv_stream_t stream);
 
+/* Append `tokens` new rows per head to the exact (residual) window, in place:
+ * keys[h][offset + t] = keys_new[h][t], the same for values, one launch for
+ * both.  Replaces the torch.cat pair of models/quantized_kv.py:109-110
+ * (`append_for_attention`) when the window lives in a buffer with spare
+ * capacity.  16-bit elements; rows must be dense and 16-byte aligned
+ * (strides in elements, multiples of 8). */
+typedef struct {
+  const void *keys_new;   /* [H][tokens][D] */
+  const void *values_new;
+  int64_t kn_stride_head, kn_stride_token;
+  int64_t vn_stride_head, vn_stride_token;
+  void *keys;             /* window buffers [H][capacity][D] */
+  void *values;
+  int64_t k_stride_head, k_stride_token;
+  int64_t v_stride_head, v_stride_token;
+  int32_t heads, tokens, head_dim, offset;
+} ckv_residual_args;
+
+int ckv_residual_append(const ckv_residual_args *args, ckv_stream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Attention over a compressed view                                         */
 /* ---------------------------------------------------------------------- */

@@ -218,3 +218,38 @@ def test_long_decode_loop_never_gives_up_a_wait():
                 layer.compact_residual()
         torch.cuda.synchronize()
     assert attention_error() == 0
+
+
+def test_window_appends_in_place_and_keeps_earlier_views():
+    """The exact window is written in place (no torch.cat per token).  It must
+    equal the concatenation the reference keeps, views handed out earlier
+    must not change, and a rolled-back snapshot must be appendable again."""
+    from trpg_b200.quantized_kv import QuantizedAttentionLayer
+    gen = torch.Generator(device='cuda').manual_seed(8)
+    with torch.inference_mode():
+        k0 = torch.randn(1, 2, 700, 128, generator=gen, device='cuda').bfloat16()
+        layer = QuantizedAttentionLayer(8)
+        layer.update(k0, -k0)
+        ref_k, ref_v = layer.keys.clone(), layer.values.clone()
+        views = []
+        for step in range(300):        # crosses compactions
+            x = torch.randn(1, 2, 1, 128, generator=gen, device='cuda').bfloat16()
+            view = layer.append_for_attention(x, 2 * x)
+            ref_k, ref_v = torch.cat((ref_k, x), -2), torch.cat((ref_v, 2 * x), -2)
+            assert torch.equal(view.keys, ref_k) and torch.equal(view.values, ref_v)
+            views.append((view.keys, view.keys.clone()))
+            before = layer.keys.shape[-2]
+            layer.compact_residual()
+            drop = before - layer.keys.shape[-2]
+            ref_k, ref_v = ref_k[..., drop:, :], ref_v[..., drop:, :]
+        for live, copy in views:
+            assert torch.equal(live, copy)
+        # rollback: restore an earlier window view and append different tokens
+        snap = (layer.keys, layer.values, layer.cumulative_length)
+        y = torch.randn(1, 2, 1, 128, generator=gen, device='cuda').bfloat16()
+        first = layer.append_for_attention(y, y).keys.clone()
+        layer.keys, layer.values, layer.cumulative_length = snap
+        z = torch.randn(1, 2, 1, 128, generator=gen, device='cuda').bfloat16()
+        again = layer.append_for_attention(z, z)
+        assert torch.equal(again.keys[..., :-1, :], first[..., :-1, :])
+        assert torch.equal(again.keys[..., -1:, :], z)

@@ -98,13 +98,19 @@ def attention(queries: Sequence[torch.Tensor], views: Sequence, scale: float, *,
     return out
 
 
+_decode_op = None
+
+
 def _single(query, view, scale):
+    """One sequence over its whole view; the op fixes any bank or window
+    layout the kernel cannot read directly."""
+    global _decode_op
     if view.packed_tokens < 128 or view.keys.shape[2] == 0:
         return attention([query], [view], scale)[0]
-    return ops().decode(query, _inner_dense(view.key_data), _inner_dense(view.key_meta),
-                        _dense_rows(view.value_data), _dense_rows(view.value_meta),
-                        _residual(view.keys), _residual(view.values), int(view.packed_tokens),
-                        int(view.length), int(view.bits), float(scale))
+    if _decode_op is None:
+        _decode_op = ops().decode
+    return _decode_op(query, view.key_data, view.key_meta, view.value_data, view.value_meta,
+                      view.keys, view.values, view.packed_tokens, view.length, view.bits, scale)
 
 
 def decode(query: torch.Tensor, view, scale: float) -> torch.Tensor:

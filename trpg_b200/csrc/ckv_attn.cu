@@ -736,6 +736,48 @@ int encode_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   return CKV_OK;
 }
 
+// Encoded tensor maps of recent calls, per host thread: a decode loop passes
+// the same banks call after call (they change only when a slab grows or a
+// block is compacted), and encoding costs more than a lookup.
+struct MapKey {
+  const void *kd, *vd;
+  int64_t kd_u, kd_h, vd_t, vd_h;
+  int32_t unit_end, hkv, bits, d;
+  bool operator==(const MapKey &o) const {
+    return kd == o.kd && vd == o.vd && kd_u == o.kd_u && kd_h == o.kd_h && vd_t == o.vd_t &&
+           vd_h == o.vd_h && unit_end == o.unit_end && hkv == o.hkv && bits == o.bits && d == o.d;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap tk, tv;
+  bool used = false;
+};
+
+template <int BITS, int D>
+int cached_maps(const ckv_seq &s, int hkv, SeqDev &d) {
+  constexpr int N = 16;
+  thread_local MapEntry cache[N];
+  thread_local int next = 0;
+  const MapKey key{s.key_data, s.value_data, s.kd_stride_unit, s.kd_stride_head, s.vd_stride_token,
+                   s.vd_stride_head, s.unit_end, hkv, BITS, D};
+  for (int i = 0; i < N; ++i)
+    if (cache[i].used && cache[i].key == key) {
+      d.tk = cache[i].tk;
+      d.tv = cache[i].tv;
+      return CKV_OK;
+    }
+  const int st = encode_maps<BITS, D>(s, hkv, d);
+  if (st != CKV_OK) return st;
+  MapEntry &e = cache[next];
+  next = (next + 1) % N;
+  e.key = key;
+  e.tk = d.tk;
+  e.tv = d.tv;
+  e.used = true;
+  return CKV_OK;
+}
+
 template <int BITS, int D, int NT, int DT, int MAXS>
 int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
   using C = Cfg<BITS, D, NT>;
@@ -766,7 +808,7 @@ int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st)
     SeqDev &d = p.seq[i];
     d.q = s.query; d.q_h = s.q_stride_head; d.q_n = s.q_stride_pos;
     if (s.unit_end > s.unit_begin) {
-      const int st = encode_maps<BITS, D>(s, a.heads_kv, d);
+      const int st = cached_maps<BITS, D>(s, a.heads_kv, d);
       if (st != CKV_OK) return st;
     }
     d.km = s.key_meta; d.km_h = s.km_stride_head; d.km_u = s.km_stride_unit;

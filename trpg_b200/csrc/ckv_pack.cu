@@ -198,6 +198,19 @@ __global__ void __launch_bounds__(256) append_kernel(ckv_append_args a) {
   }
 }
 
+// In-place append to the exact window.  Grid: heads x tokens; block: one
+// thread per 16-byte piece of a row (D / 8), copying that piece of the key
+// row and of the value row.
+__global__ void residual_append_kernel(ckv_residual_args a) {
+  const int h = blockIdx.x / a.tokens, t = blockIdx.x % a.tokens, k = threadIdx.x;
+  const uint16_t *kn = static_cast<const uint16_t *>(a.keys_new) + h * a.kn_stride_head + t * a.kn_stride_token;
+  const uint16_t *vn = static_cast<const uint16_t *>(a.values_new) + h * a.vn_stride_head + t * a.vn_stride_token;
+  uint16_t *kd = static_cast<uint16_t *>(a.keys) + h * a.k_stride_head + int64_t(a.offset + t) * a.k_stride_token;
+  uint16_t *vd = static_cast<uint16_t *>(a.values) + h * a.v_stride_head + int64_t(a.offset + t) * a.v_stride_token;
+  reinterpret_cast<uint4 *>(kd)[k] = reinterpret_cast<const uint4 *>(kn)[k];
+  reinterpret_cast<uint4 *>(vd)[k] = reinterpret_cast<const uint4 *>(vn)[k];
+}
+
 bool aligned(const void *p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
 template <int DT, int BITS>
@@ -298,4 +311,24 @@ extern "C" int ckv_pack_append(const ckv_append_args *args, ckv_stream_t stream)
   if (a.dtype == CKV_BF16)
     return a.bits == 8 ? launch_append<CKV_BF16, 8>(a, s) : launch_append<CKV_BF16, 4>(a, s);
   return a.bits == 8 ? launch_append<CKV_F16, 8>(a, s) : launch_append<CKV_F16, 4>(a, s);
+}
+
+extern "C" int ckv_residual_append(const ckv_residual_args *args, ckv_stream_t stream) {
+  if (!args) return CKV_ERR_INVALID;
+  const ckv_residual_args &a = *args;
+  if (a.heads < 1 || a.tokens < 0 || a.offset < 0 || a.head_dim < 8 || a.head_dim % 8 ||
+      a.head_dim > 1024)
+    return CKV_ERR_INVALID;
+  if (a.tokens == 0) return CKV_OK;
+  if (!a.keys_new || !a.values_new || !a.keys || !a.values) return CKV_ERR_INVALID;
+  if (!aligned(a.keys_new, 16) || !aligned(a.values_new, 16) || !aligned(a.keys, 16) ||
+      !aligned(a.values, 16))
+    return CKV_ERR_INVALID;
+  for (int64_t st : {a.kn_stride_head, a.kn_stride_token, a.vn_stride_head, a.vn_stride_token,
+                     a.k_stride_head, a.k_stride_token, a.v_stride_head, a.v_stride_token})
+    if (st % 8) return CKV_ERR_INVALID;
+  if (int64_t(a.heads) * a.tokens > (int64_t(1) << 31) - 1) return CKV_ERR_INVALID;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  residual_append_kernel<<<unsigned(a.heads * a.tokens), unsigned(a.head_dim / 8), 0, s>>>(a);
+  return cuda_status(cudaGetLastError());
 }

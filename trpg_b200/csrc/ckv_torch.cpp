@@ -145,6 +145,78 @@ void pack_append(const Tensor &keys, const Tensor &values, const Tensor &kd, con
   check_status(ckv_pack_append(&a, current_stream(keys)), "pack_append");
 }
 
+// Layouts the kernels need.  A tensor that already has it passes through; any
+// other (a strided view, a misaligned base) is copied once here.
+bool aligned16(const Tensor &t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0; }
+
+Tensor fit_copy(const Tensor &t) {
+  Tensor c = t.contiguous();
+  return aligned16(c) ? c : c.clone();
+}
+
+// Bank tensor: the last `dense` dims packed densely, 16-byte aligned base.
+Tensor fit_bank(const Tensor &t, int dense) {
+  if (!t.defined()) return t;
+  const int64_t d = t.dim();
+  bool ok = d >= dense && t.stride(d - 1) == 1 && aligned16(t);
+  int64_t expect = t.size(d - 1);
+  for (int k = 2; ok && k <= dense; ++k) {
+    ok = t.stride(d - k) == expect;
+    expect *= t.size(d - k);
+  }
+  return ok ? t : fit_copy(t);
+}
+
+// Rows of 16-bit values: last dim dense, head and token strides multiples of
+// 8 elements (16-byte rows), 16-byte aligned base.
+Tensor fit_rows(const Tensor &t) {
+  if (!t.defined() || t.dim() != 4) return t;
+  const bool ok = t.stride(3) == 1 && t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0 && aligned16(t);
+  return ok ? t : fit_copy(t);
+}
+
+// keys[:, :, offset:offset+n] = keys_new (and values) for window buffers
+// [1,H,C,D] with capacity C >= offset + n; one launch.
+void residual_append(const Tensor &keys_new, const Tensor &values_new, const Tensor &keys,
+                     const Tensor &values, int64_t offset) {
+  for (auto *t : {&keys_new, &values_new, &keys, &values}) require_cuda(*t, "residual tensor");
+  TORCH_CHECK(keys_new.dim() == 4 && values_new.sizes() == keys_new.sizes() && keys_new.size(0) == 1,
+              "ckv::residual_append: new rows must be [1,H,n,D]");
+  TORCH_CHECK(keys.dim() == 4 && values.sizes() == keys.sizes() && keys.size(0) == 1 &&
+                  keys.size(1) == keys_new.size(1) && keys.size(3) == keys_new.size(3),
+              "ckv::residual_append: window buffers must be [1,H,C,D]");
+  for (auto *t : {&values_new, &keys, &values}) {
+    TORCH_CHECK(t->scalar_type() == keys_new.scalar_type(), "ckv::residual_append: dtype mismatch");
+    TORCH_CHECK(t->device() == keys_new.device(), "ckv::residual_append: device mismatch");
+  }
+  TORCH_CHECK(offset >= 0 && offset + keys_new.size(2) <= keys.size(2),
+              "ckv::residual_append: window capacity exceeded");
+  c10::cuda::CUDAGuard guard(keys.device());
+  const Tensor kn = fit_rows(keys_new), vn = fit_rows(values_new);
+  ckv_residual_args a{};
+  a.keys_new = kn.data_ptr();
+  a.values_new = vn.data_ptr();
+  a.kn_stride_head = kn.stride(1);
+  a.kn_stride_token = kn.stride(2);
+  a.vn_stride_head = vn.stride(1);
+  a.vn_stride_token = vn.stride(2);
+  a.keys = keys.data_ptr();
+  a.values = values.data_ptr();
+  a.k_stride_head = keys.stride(1);
+  a.k_stride_token = keys.stride(2);
+  a.v_stride_head = values.stride(1);
+  a.v_stride_token = values.stride(2);
+  a.heads = int(keys.size(1));
+  a.tokens = int(keys_new.size(2));
+  a.head_dim = int(keys.size(3));
+  a.offset = int(offset);
+  TORCH_CHECK(keys.stride(3) == 1 && values.stride(3) == 1 && aligned16(keys) && aligned16(values) &&
+                  keys.stride(1) % 8 == 0 && keys.stride(2) % 8 == 0 && values.stride(1) % 8 == 0 &&
+                  values.stride(2) % 8 == 0,
+              "ckv::residual_append: window buffers need dense, 16-byte aligned rows");
+  check_status(ckv_residual_append(&a, current_stream(keys)), "residual_append");
+}
+
 // ---------------------------------------------------------------------------
 // Attention
 // ---------------------------------------------------------------------------
@@ -272,6 +344,8 @@ std::vector<Tensor> attention(const std::vector<Tensor> &queries, const std::vec
   c10::cuda::CUDAGuard guard(q0.device());
   std::vector<ckv_seq> seqs(n);
   std::vector<Tensor> outs(n);
+  std::vector<Tensor> keep;   // layout copies made for this call
+  keep.reserve(6 * n);
   for (size_t i = 0; i < n; ++i) {
     const Tensor &q = queries[i];
     TORCH_CHECK(q.device() == q0.device() && q.scalar_type() == q0.scalar_type() &&
@@ -280,7 +354,16 @@ std::vector<Tensor> attention(const std::vector<Tensor> &queries, const std::vec
     for (const Tensor *t : {&kd[i], &km[i], &vd[i], &vm[i], &rk[i], &rv[i]})
       TORCH_CHECK(!t->defined() || t->device() == q0.device(),
                   "ckv::attention: all tensors must be on the query's device");
-    seqs[i] = make_seq(q, kd[i], km[i], vd[i], vm[i], rk[i], rv[i], packed[i], lengths[i],
+    const bool has_packed = ranges[4 * i + 1] > ranges[4 * i];
+    const bool has_resid = ranges[4 * i + 3] > ranges[4 * i + 2];
+    keep.push_back(has_packed ? fit_bank(kd[i], 2) : Tensor());
+    keep.push_back(has_packed ? fit_bank(km[i], 2) : Tensor());
+    keep.push_back(has_packed ? fit_bank(vd[i], 3) : Tensor());
+    keep.push_back(has_packed ? fit_bank(vm[i], 3) : Tensor());
+    keep.push_back(has_resid ? fit_rows(rk[i]) : Tensor());
+    keep.push_back(has_resid ? fit_rows(rv[i]) : Tensor());
+    const Tensor *f = &keep[keep.size() - 6];
+    seqs[i] = make_seq(q, f[0], f[1], f[2], f[3], f[4], f[5], packed[i], lengths[i],
                        &ranges[4 * i], bits, hkv);
     outs[i] = partial ? at::empty({hq * nq, D + 2}, q.options().dtype(at::kFloat))
                       : at::empty({1, hq, nq, D}, q.options());
@@ -323,8 +406,10 @@ Tensor decode(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor 
   c10::cuda::CUDAGuard guard(q.device());
   const int64_t range[4] = {0, packed / 128, 0, rk.size(2)};
   const int64_t hkv = rk.size(1);
+  const Tensor kd2 = fit_bank(kd, 2), km2 = fit_bank(km, 2), vd2 = fit_bank(vd, 3),
+               vm2 = fit_bank(vm, 3), rk2 = fit_rows(rk), rv2 = fit_rows(rv);
   std::vector<ckv_seq> seqs(1);
-  seqs[0] = make_seq(q, kd, km, vd, vm, rk, rv, packed, length, range, bits, hkv);
+  seqs[0] = make_seq(q, kd2, km2, vd2, vm2, rk2, rv2, packed, length, range, bits, hkv);
   Tensor out = at::empty_like(q, at::MemoryFormat::Contiguous);
   seqs[0].out = out.data_ptr();
   run_attention(seqs, q, q.size(1), hkv, q.size(3), q.size(2), bits, scale, false);
@@ -388,6 +473,8 @@ TORCH_LIBRARY(ckv, m) {
       "decode(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
       "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
   m.def("attention_error(Tensor like) -> int");
+  m.def("residual_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
+        "int offset) -> ()");
 }
 
 namespace {
@@ -423,4 +510,5 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("combine_partials", &combine_partials);
   m.impl("decode", &decode);
   m.impl("attention_error", &attention_error);
+  m.impl("residual_append", &residual_append);
 }

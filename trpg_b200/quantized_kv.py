@@ -11,10 +11,20 @@ working unchanged:
   (``:93-159``): exact residual window, append / compact / update.
 * ``make_cache`` / ``cache_bytes`` (``:162-188``).
 
-What changes is the quantize-on-append step: ``compact_residual`` quantizes
-the compacted tokens straight into the bank slabs with one launch
-(``ckv_pack_append``) instead of packing into temporaries and copying.  The
-bytes written are identical to packing the same rows with ``_pack``.
+Two steps change:
+
+* quantize-on-append: ``compact_residual`` quantizes the compacted tokens
+  straight into the bank slabs with one launch (``ckv_pack_append``) instead
+  of packing into temporaries and copying.  The bytes written are identical
+  to packing the same rows with ``_pack``.
+* the exact window: instead of ``torch.cat`` of the whole window on every
+  token (``models/quantized_kv.py:109-110``), the window lives in a buffer
+  with spare capacity and new tokens are written in place, K and V in one
+  launch (``ckv_residual_append``).  ``keys`` / ``values`` are views of its
+  first R rows; earlier views are never written again (appends go past
+  their end, and compaction moves the rest to a new buffer), so snapshots
+  taken by ``HybridCacheTransaction`` stay valid.  A rolled-back view that
+  is appended to again takes the place of the discarded tokens.
 
 CUDA tensors only: the quantizer and dequantizer have no CPU path here.
 """
@@ -30,7 +40,20 @@ from . import quantized_kv_kernels as _kernels
 from ._native import ROUNDING, ops
 
 KEY_SLAB_UNITS = 32       # models/quantized_kv.py:48
+WINDOW_MIN = 512          # tokens of exact-window capacity (compaction keeps it under 256)
 VALUE_SLAB_TOKENS = 4096  # models/quantized_kv.py:51
+
+
+_residual_append_op = None
+
+
+def _residual_append(keys_new, values_new, kb, vb, offset):
+    """One launch writes the new key and value rows into the window buffers
+    (the op copies rows it cannot read directly)."""
+    global _residual_append_op
+    if _residual_append_op is None:
+        _residual_append_op = ops().residual_append
+    _residual_append_op(keys_new, values_new, kb, vb, offset)
 
 
 def _pack(rows, bits, rounding=None):
@@ -128,29 +151,83 @@ class QuantizedAttentionLayer(DynamicLayer):
         self.bits = bits
         self.rounding = rounding or _kernels.DEFAULT_ROUNDING
         self.cumulative_length = 0
+        self._window = None   # (key buffer, value buffer, keys view, values view, rows, capacity)
         self.key_bank = _PackedBank(bits, 'key', self.rounding)
         self.value_bank = _PackedBank(bits, 'value', self.rounding)
 
     def append_for_attention(self, key_states, value_states):
-        """``models/quantized_kv.py:103-114``."""
+        """``models/quantized_kv.py:103-114``, appending in place to the window buffer."""
+        n = key_states.shape[-2]
+        w = self._window
+        if w is not None and self.keys is w[2] and self.values is w[3] and w[4] + n <= w[5]:
+            # Fast path: keys / values are the views this layer made last time
+            # (the op checks dtype and device).
+            r = w[4]
+            _residual_append(key_states, value_states, w[0], w[1], r)
+            self._set_window(w[0], w[1], r + n)
+            self.cumulative_length += n
+            return QuantizedKVView(self.key_bank.data, self.key_bank.meta, self.value_bank.data,
+                                   self.value_bank.meta, self.key_bank.units * 128, self.keys,
+                                   self.values, self.bits, self.cumulative_length)
         if key_states.shape[-1] % 64 or value_states.shape[-1] % 64:
             raise ValueError('quantized KV needs head_dim to be a multiple of 64')
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
-        self.cumulative_length += key_states.shape[-2]
-        self.keys = torch.cat((self.keys, key_states), dim=-2)
-        self.values = torch.cat((self.values, value_states), dim=-2)
+        self.cumulative_length += n
+        if not (key_states.is_cuda and key_states.dim() == 4 and key_states.shape[0] == 1
+                and key_states.dtype in (torch.bfloat16, torch.float16)
+                and value_states.shape == key_states.shape and value_states.dtype == key_states.dtype):
+            self.keys = torch.cat((self.keys, key_states), dim=-2)
+            self.values = torch.cat((self.values, value_states), dim=-2)
+            self._window = None
+        else:
+            kb, vb = self._window_for(key_states, n)
+            r = self.keys.shape[-2] if self.keys.dim() == 4 else 0
+            _residual_append(key_states, value_states, kb, vb, r)
+            self._set_window(kb, vb, r + n)
         return QuantizedKVView(self.key_bank.data, self.key_bank.meta,
                                self.value_bank.data, self.value_bank.meta,
                                self.key_bank.units * 128, self.keys, self.values,
                                self.bits, self.cumulative_length)
+
+    def _set_window(self, kb, vb, r):
+        """keys / values = the first r rows of the window buffers."""
+        self.keys, self.values = kb.narrow(2, 0, r), vb.narrow(2, 0, r)
+        self._window = (kb, vb, self.keys, self.values, r, kb.shape[2])
+
+    def _window_for(self, like, n):
+        """Window buffers that hold ``keys`` / ``values`` as their first rows and
+        have room for ``n`` more; a new pair (with the current rows copied) when
+        the current window is full or ``keys`` is not a prefix of it."""
+        window = self._window
+        r = self.keys.shape[-2] if self.keys.dim() == 4 else 0
+        if window is not None:
+            kb, vb = window[0], window[1]
+            if (self.keys.dim() == 4 and self.keys.data_ptr() == kb.data_ptr()
+                    and self.values.data_ptr() == vb.data_ptr() and self.keys.stride() == kb.stride()
+                    and self.values.stride() == vb.stride() and r + n <= kb.shape[2]
+                    and kb.dtype == like.dtype and kb.device == like.device
+                    and kb.shape[1] == like.shape[1] and kb.shape[3] == like.shape[3]):
+                return kb, vb
+        return self._new_window(like, r + n, self.keys if r else None, self.values if r else None)
+
+    def _new_window(self, like, need, keys=None, values=None):
+        b, h, _, d = like.shape
+        cap = max(WINDOW_MIN, -(-need // 128) * 128 + 256)   # room for 256 more tokens
+        kb = torch.empty((b, h, cap, d), dtype=like.dtype, device=like.device)
+        vb = torch.empty_like(kb)
+        if keys is not None:
+            kb[:, :, :keys.shape[2]].copy_(keys)
+            vb[:, :, :values.shape[2]].copy_(values)
+        self._window = (kb, vb, None, None, 0, cap)
+        return kb, vb
 
     def compact_residual(self):
         """``models/quantized_kv.py:116-124``, quantizing straight into the slabs."""
         count = max(0, (self.keys.shape[-2] - 128) // 128 * 128)
         if not count:
             return
-        b, h, _, d = self.keys.shape
+        b, h, r, d = self.keys.shape
         if b != 1:
             raise NotImplementedError('the quantized hybrid cache holds a single session')
         units = self.key_bank.units
@@ -161,8 +238,11 @@ class QuantizedAttentionLayer(DynamicLayer):
                           ROUNDING[self.rounding])
         self.key_bank.units = units + count // 128
         self.value_bank.units = units + count // 128
-        self.keys = self.keys[..., count:, :].clone()
-        self.values = self.values[..., count:, :].clone()
+        # The rest moves to a new window (the reference clones it); the old
+        # buffer, and every view of it handed out, stays as it was.
+        kb, vb = self._new_window(self.keys, r - count, self.keys[..., count:, :],
+                                  self.values[..., count:, :])
+        self._set_window(kb, vb, r - count)
 
     def update(self, key_states, value_states, *args, **kwargs):
         """``models/quantized_kv.py:126-134``: dequantized history + residual."""
