@@ -425,6 +425,156 @@ def b200_arm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# The other configurations (parity-test cases; measured on request)
+# ---------------------------------------------------------------------------
+WORKLOADS = {
+    'c3': 'batched decode: 64 sequences, ragged contexts uniform in [1024, 8192], Q8, one query '
+          'token each, 16q/4kv x 256, one launch per GPU; sequences sharded over GPUs by LPT on bytes',
+    'c4': 'MTP verification: 16 sequences x 4 query tokens (lower-right causal), 16384 context, Q8, '
+          '16q/4kv x 256, one launch per GPU; sequences sharded over GPUs',
+    'c5': 'long-context Q4 decode: 1 sequence, 131072 context, 16q/4kv x 256; split-KV over GPUs, '
+          '(m, l, o) partials all-gathered over NCCL and merged',
+}
+
+
+def build_view(gen, length, n_new, bits, device):
+    """Reference-reachable cache state: update(L - n) then append(n)."""
+    from trpg_b200.quantized_kv import QuantizedAttentionLayer
+    with torch.inference_mode():
+        k, v = synthetic_kv(gen, length - n_new, device)
+        layer = QuantizedAttentionLayer(bits)
+        layer.update(k, v)
+        del k, v
+        kn = torch.randn(1, HKV, n_new, D, generator=gen, device=device).bfloat16()
+        vn = torch.randn(1, HKV, n_new, D, generator=gen, device=device).bfloat16()
+        view = layer.append_for_attention(kn, vn)
+    return layer, view
+
+
+def view_bytes_q(view, nq=1) -> int:
+    """Algorithmic bytes of one attention call over `view`: codes + meta,
+    exact window, query and output."""
+    bits = view.bits
+    per_token = 2 * D * bits // 8 + D * 8 // 128 + (D // 64) * 8
+    return HKV * (view.packed_tokens * per_token + view.keys.shape[2] * 2 * D * 2) + 2 * HQ * nq * D * 2
+
+
+def graph_seconds(fn, replays=20):
+    """Device seconds per call of `fn`, from a CUDA graph of one call replayed
+    back to back between events on the capturing stream."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.inference_mode():
+        with torch.cuda.stream(stream):
+            fn()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                graph.replay()
+            a.record(stream)
+            for _ in range(replays):
+                graph.replay()
+            b.record(stream)
+        stream.synchronize()
+        del graph
+    return a.elapsed_time(b) * 1e-3 / replays
+
+
+def extra_workload(args, world, rank, local):
+    from trpg_b200 import _native
+    from trpg_b200.compressed_kv_kernels import attention, combine
+    from trpg_b200.sharding import lpt_partition, split_kv_range, view_bytes
+    _native.load()
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    peak, peak_kind = peaks()
+    w = args.workload
+    clocks = Clocks(local)
+    if w in ('c3', 'c4'):
+        if w == 'c3':
+            cpu = torch.Generator().manual_seed(3)
+            lengths = torch.randint(1024, 8193, (64,), generator=cpu).tolist()
+            nq, bits = 1, 8
+        else:
+            lengths, nq, bits = [16384] * 16, 4, 8
+        # Shard by bytes (the state rule gives P and R from L).
+        def pr(length):
+            p = 128 * max(0, (length - nq - 128) // 128)
+            return p, length - p
+        parts = lpt_partition([view_bytes(*pr(L), HKV, D, bits) for L in lengths], world)
+        mine = parts[rank]
+        gen.manual_seed(1000 * (3 if w == 'c3' else 4) + rank)
+        views, queries = [], []
+        for i in mine:
+            _, view = build_view(gen, lengths[i], nq, bits, device)
+            views.append(view)
+            queries.append(torch.randn(1, HQ, nq, D, generator=gen, device=device).bfloat16())
+        fn = lambda: attention(queries, views, SCALE)
+        nbytes = sum(view_bytes_q(v, nq) for v in views)
+        tokens = len(lengths) * nq
+    elif w == 'c5':
+        gen.manual_seed(5)
+        _, view = build_view(gen, 131072, 1, 4, device)
+        q = torch.randn(1, HQ, 1, D, generator=gen, device=device).bfloat16()
+        units, resid = view.packed_tokens // 128, view.keys.shape[2]
+        rng = split_kv_range(units, resid, world, rank)
+        if world == 1:
+            fn = lambda: attention([q], [view], SCALE)
+        else:
+            fn = lambda: attention([q], [view], SCALE, ranges=[rng], partial=True)
+        per_token = 2 * D * 4 // 8 + D * 8 // 128 + (D // 64) * 8
+        nbytes = HKV * ((rng[1] - rng[0]) * 128 * per_token + (rng[3] - rng[2]) * 2 * D * 2) + 2 * HQ * D * 2
+        tokens = 1
+    else:
+        raise SystemExit(f'unknown workload {w}')
+    sec_kernel = graph_seconds(fn)
+    # Whole step (for c5 on several GPUs: partial + NCCL all-gather + merge),
+    # device-timed over the steps, max over ranks.
+    if w == 'c5' and world > 1:
+        import torch.distributed as dist
+        def step():
+            part = fn()[0]
+            out = torch.empty((world * part.shape[0], part.shape[1]), dtype=part.dtype, device=device)
+            dist.all_gather_into_tensor(out, part)
+            return combine(out.view(world, *part.shape), torch.bfloat16)
+    else:
+        step = fn
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        clocks.start()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        clocks.stop()
+        barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    k_us = max_over_ranks(sec_kernel * 1e6, world)
+    achieved = nbytes / sec_kernel / 1e9
+    line = {'metric': f'{w}: decode attention tokens/s', 'workload': WORKLOADS[w], 'value': tokens / (ms * 1e-3),
+            'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': ms, 'higher_is_better': True,
+            'scaling': 'strong' if w == 'c5' else 'strong (fixed batch sharded)',
+            'dtype': 'u4/bf16' if w == 'c5' else 'u8/bf16', 'data': 'synthetic',
+            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
+                         'frac': achieved / peak, 'peak_source': peak_kind,
+                         'bytes_per_launch_rank0': nbytes, 'us_per_launch_max_rank': k_us},
+            'clocks': clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -433,6 +583,9 @@ def main():
     ap.add_argument('--impl', choices=('b200', 'reference'), default='b200')
     ap.add_argument('--cpu-steps', type=int, default=24)
     ap.add_argument('--no-cpu', action='store_true')
+    ap.add_argument('--workload', choices=('c2',) + tuple(WORKLOADS), default='c2',
+                    help='c2 (default) is the headline 32K decode step; c3/c4/c5 measure the '
+                         'other configurations')
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
@@ -440,6 +593,8 @@ def main():
     try:
         if args.impl == 'reference':
             reference_arm(args, world, rank)
+        elif args.workload != 'c2':
+            extra_workload(args, world, rank, local)
         else:
             b200_arm(args, world, rank, local)
     finally:
