@@ -94,15 +94,58 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     mbar_fence_init();
   }
   __syncthreads();
-  if (tid == PRODUCER * 32) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.seq[s_seq].tk) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.seq[s_seq].tv) : "memory");
-  }
+  // The next kernel in the stream may launch now; its CTAs start as this
+  // grid's CTAs exit.
+  pdl_trigger();
   const int seq = s_seq;
   const SeqDev &sd = p.seq[seq];
   const int local = cta - sd.cta_begin;
   const int head = local / sd.cph, split = local % sd.cph;
   const int G = p.group, rows = p.rows, nq = p.nq;
+
+  // This CTA's items: packed units [ub, ue) then residual chunks of RCHUNK tokens.
+  const int np = sd.ue - sd.ub;
+  const int nr = (sd.re - sd.rb + RCHUNK - 1) / RCHUNK;
+  const int ni = np + nr;
+  const int ib = int(int64_t(split) * ni / sd.cph);
+  const int n = int(int64_t(split + 1) * ni / sd.cph) - ib;
+
+  // Producer side of one packed item: stage st of the K (kchain) or V ring.
+  auto issue_packed = [&](bool kchain, int i, int st) {
+    const int unit = sd.ub + ib + i;
+    if (kchain) {
+      const uint32_t dst = sbase + C::OFF_K + st * C::KST, fb = bar(KFULL + st);
+      mbar_expect_tx(fb, C::KCODE + C::KMETA);
+      tma_load_4d(dst, &sd.tk, fb, 0, 0, unit, head);
+      bulk_load(dst + C::KCODE, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, fb);
+    } else {
+      const uint32_t dst = sbase + C::OFF_V + st * C::VST, fb = bar(VFULL + st);
+      mbar_expect_tx(fb, C::VCODE + C::VMETA);
+#pragma unroll
+      for (int bx = 0; bx < C::NVB; ++bx)
+        tma_load_3d(dst + bx * 128 * C::VBOX, &sd.tv, fb, bx * C::VBOX, unit * 128, head);
+      bulk_load(dst + C::VCODE, sd.vm + head * sd.vm_h + int64_t(unit) * 128 * sd.vm_t, C::VMETA, fb);
+    }
+  };
+
+  // Before waiting for the previous kernel, each producer starts the first
+  // packed block: the banks are never written by a kernel of this library
+  // that lets its successor start early, so they are complete already.
+  // Everything else (query, exact window, workspace, output) comes after the
+  // wait.
+  int preissued = 0;
+  if (warp >= PRODUCER) {
+    const bool kchain = warp == PRODUCER;
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(kchain ? &sd.tk : &sd.tv) : "memory");
+      if (n > 0 && ib < np) {
+        issue_packed(kchain, 0, 0);
+        s_issued[kchain ? 0 : NK] = 0;
+      }
+    }
+    preissued = (n > 0 && ib < np) ? 1 : 0;
+  }
+  pdl_wait();
 
   // Query B fragments (channel order of the MMA k index), filled by the QK
   // warps while the producers start streaming.
@@ -122,12 +165,6 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     named_sync(BAR_QFRAG, QK_WARPS * 32);
   }
 
-  // This CTA's items: packed units [ub, ue) then residual chunks of RCHUNK tokens.
-  const int np = sd.ue - sd.ub;
-  const int nr = (sd.re - sd.rb + RCHUNK - 1) / RCHUNK;
-  const int ni = np + nr;
-  const int ib = int(int64_t(split) * ni / sd.cph);
-  const int n = int(int64_t(split + 1) * ni / sd.cph) - ib;
   auto fail = [&]() {
     atomicOr(p.error, 1u);
     s_abort = 1;
@@ -147,8 +184,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     const uint32_t ring = sbase + (kchain ? C::OFF_K : C::OFF_V);
     const T *res = static_cast<const T *>(kchain ? sd.rk : sd.rv);
     const int64_t res_h = kchain ? sd.rk_h : sd.rv_h, res_t = kchain ? sd.rk_t : sd.rv_t;
-    int issued = 0;
-    for (int i = 0; i < n; ++i) {
+    int issued = preissued;
+    for (int i = preissued; i < n; ++i) {
       const int st = i % depth;
       // One lane decides for the warp so that all lanes take the same path.
       int go = 0;
@@ -163,21 +200,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       const uint32_t dst = ring + st * stage_bytes, fb = bar(full0 + st);
       const int it = ib + i;
       if (it < np) {
-        if (lane == 0) {
-          const int unit = sd.ub + it;
-          if (kchain) {
-            mbar_expect_tx(fb, C::KCODE + C::KMETA);
-            tma_load_4d(dst, &sd.tk, fb, 0, 0, unit, head);
-            bulk_load(dst + C::KCODE, sd.km + head * sd.km_h + int64_t(unit) * sd.km_u, C::KMETA, fb);
-          } else {
-            mbar_expect_tx(fb, C::VCODE + C::VMETA);
-#pragma unroll
-            for (int bx = 0; bx < C::NVB; ++bx)
-              tma_load_3d(dst + bx * 128 * C::VBOX, &sd.tv, fb, bx * C::VBOX, unit * 128, head);
-            bulk_load(dst + C::VCODE, sd.vm + head * sd.vm_h + int64_t(unit) * 128 * sd.vm_t, C::VMETA,
-                      fb);
-          }
-        }
+        if (lane == 0) issue_packed(kchain, i, st);
       } else {
         // Residual chunk: 16-byte cp.async by every lane into rows of pitch
         // RP.  Rows past the window's end repeat its last token (finite
@@ -822,8 +845,21 @@ int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st)
     d.cta_begin = pl.cta_begin[i];
     d.cph = pl.cph[i];
   }
-  kern<<<pl.grid, THREADS, C::SMEM, st>>>(p);
-  return cuda_status(cudaGetLastError());
+  // Programmatic stream serialization: this grid may start while the
+  // previous kernel in the stream finishes (the kernel waits for it before
+  // touching anything that kernel could have written).
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+  return CKV_OK;
 }
 
 template <int BITS, int D, int NT, int DT>

@@ -202,6 +202,12 @@ __global__ void __launch_bounds__(256) append_kernel(ckv_append_args a) {
 // thread per 16-byte piece of a row (D / 8), copying that piece of the key
 // row and of the value row.
 __global__ void residual_append_kernel(ckv_residual_args a) {
+  // Let the next kernel (typically the attention call over this window)
+  // launch at once, but finish only after the previous kernel has: the new
+  // rows may be its output, and a successor that waits for this kernel then
+  // knows the earlier one is done too.
+  pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x / a.tokens, t = blockIdx.x % a.tokens, k = threadIdx.x;
   const uint16_t *kn = static_cast<const uint16_t *>(a.keys_new) + h * a.kn_stride_head + t * a.kn_stride_token;
   const uint16_t *vn = static_cast<const uint16_t *>(a.values_new) + h * a.vn_stride_head + t * a.vn_stride_token;
@@ -329,6 +335,15 @@ extern "C" int ckv_residual_append(const ckv_residual_args *args, ckv_stream_t s
     if (st % 8) return CKV_ERR_INVALID;
   if (int64_t(a.heads) * a.tokens > (int64_t(1) << 31) - 1) return CKV_ERR_INVALID;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  residual_append_kernel<<<unsigned(a.heads * a.tokens), unsigned(a.head_dim / 8), 0, s>>>(a);
-  return cuda_status(cudaGetLastError());
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(a.heads * a.tokens));
+  cfg.blockDim = dim3(unsigned(a.head_dim / 8));
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CKV_CUDA_TRY(cudaLaunchKernelEx(&cfg, residual_append_kernel, a));
+  return CKV_OK;
 }
