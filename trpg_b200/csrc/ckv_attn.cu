@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   __shared__ volatile int s_issued[NK + NV];   // last item issued into each K, then V, stage
   // kfull[NK] kempty[NK] vfull[NV] vempty[NV] pfull[TEAMS][2] pempty[TEAMS][2]
   __shared__ __align__(8) uint64_t s_bar[2 * NK + 2 * NV + 4 * TEAMS];
+  __shared__ __align__(8) uint64_t s_mbar;   // bulk copies of the merge
   // 1024-byte aligned base: the TMA swizzle patterns repeat every 1024 bytes.
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const uint32_t sbase = smem_u32(smem);
@@ -101,14 +102,19 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const SeqDev &sd = p.seq[seq];
   const int local = cta - sd.cta_begin;
   const int head = local / sd.cph, split = local % sd.cph;
+  // Item ranges go to the splits in reverse order: the highest CTA indices
+  // start last (their SMs are the last ones the previous kernel frees), so
+  // they take the first, shortest range of packed blocks, and split 0, which
+  // starts first, takes the range that ends with the exact-window chunks.
+  const int rsplit = sd.cph - 1 - split;
   const int G = p.group, rows = p.rows, nq = p.nq;
 
   // This CTA's items: packed units [ub, ue) then residual chunks of RCHUNK tokens.
   const int np = sd.ue - sd.ub;
   const int nr = (sd.re - sd.rb + RCHUNK - 1) / RCHUNK;
   const int ni = np + nr;
-  const int ib = int(int64_t(split) * ni / sd.cph);
-  const int n = int(int64_t(split + 1) * ni / sd.cph) - ib;
+  const int ib = int(int64_t(rsplit) * ni / sd.cph);
+  const int n = int(int64_t(rsplit + 1) * ni / sd.cph) - ib;
 
   // Producer side of one packed item: stage st of the K (kchain) or V ring.
   auto issue_packed = [&](bool kchain, int i, int st) {
@@ -461,7 +467,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   }
   __syncthreads();
   float *rec = p.rec + size_t(cta) * rows * D;
-  float *recml = p.rec_ml + size_t(cta) * rows * 2;
+  const int mls = ml_stride(rows);
+  float *recml = p.rec_ml + size_t(cta) * mls;
   for (int idx = tid; idx < rows * D; idx += THREADS) {
     const int row = idx / D, d = idx % D;
     const float m0 = mrow[row], m1 = mrow[C::ROWS + row];
@@ -486,39 +493,60 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   if (tid == 0) {
     __threadfence();   // the whole CTA's record stores (ordered by the barrier) before the ticket
     const unsigned prev = atomicAdd(&p.counters[seq * p.hkv + head], 1u);
-    s_last = prev == unsigned(sd.cph - 1);
+    const bool last = prev == unsigned(sd.cph - 1);
+    // Acquire side: the other CTAs' records (released by their fences before
+    // their tickets) are visible to every thread ordered after the barrier.
+    if (last) __threadfence();
+    s_last = last;
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
 
   // ---- last CTA of the pair: merge the pair's CTA records -------------------
-  // Weights per (row, record) once, then every output element sums its
-  // records with many independent 16-byte loads in flight.
+  // The pair's records are consecutive in the workspace ([cph][rows][D] fp32,
+  // then [cph][mls] (m, l) pairs), so bulk copies bring them into the freed
+  // stage memory in a few large transfers (in chunks of `mrec` records when
+  // they do not all fit), much faster than per-thread loads through one SM.
   const int c0 = sd.cta_begin + head * sd.cph;
   const int cph = sd.cph;
-  float *s_w = reinterpret_cast<float *>(smem);   // [rows][cph] m, then weight
-  float *s_l = s_w + rows * cph;                  // [rows][cph] l
-  float *s_row = s_l + rows * cph;                // [rows] (M, L)
-  for (int idx = tid; idx < rows * cph; idx += THREADS) {
-    const int row = idx / cph, c = idx % cph;
-    const float2 ml2 =
-        __ldcg(reinterpret_cast<const float2 *>(p.rec_ml) + size_t(c0 + c) * rows + row);
-    s_w[row * cph + c] = ml2.x;
-    s_l[row * cph + c] = ml2.y;
+  constexpr int D4 = D / 4;
+  constexpr int AVAIL = NK * C::KST + NV * C::VST;
+  const int outs = rows * D4;
+  const uint32_t rec_bytes = uint32_t(rows) * D * 4;
+  const uint32_t ml_bytes = uint32_t(cph) * mls * 4;                 // a multiple of 16
+  const uint32_t ml_room = (ml_bytes + 2 * C::ROWS * 4 + 127) & ~127u;
+  const int mrec = max(1, min(cph, int((AVAIL - ml_room) / rec_bytes)));
+  const float2 *s_ml = reinterpret_cast<const float2 *>(smem);        // [cph][mls / 2]
+  float *s_row = reinterpret_cast<float *>(smem + ml_bytes);           // [ROWS] (M, L)
+  const float4 *s_rec = reinterpret_cast<const float4 *>(smem + ml_room);   // [mrec][rows][D4]
+  const uint32_t mbar = smem_u32(&s_mbar);
+  auto issue = [&](int cb, int cnt, bool with_ml) {
+    // By the issuing thread: the CTA's earlier generic writes to this shared
+    // memory and the acquired record stores of the other CTAs are ordered
+    // before the asynchronous copies.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    mbar_expect_tx(mbar, uint32_t(cnt) * rec_bytes + (with_ml ? ml_bytes : 0u));
+    bulk_load(sbase + ml_room, p.rec + size_t(c0 + cb) * rows * D, uint32_t(cnt) * rec_bytes, mbar);
+    if (with_ml) bulk_load(sbase, p.rec_ml + size_t(c0) * mls, ml_bytes, mbar);
+  };
+  if (tid == 0) {
+    mbar_init(mbar, 1);
+    mbar_fence_init();
+    issue(0, min(mrec, cph), true);
   }
   __syncthreads();
+  if (!mbar_wait(mbar, 0)) atomicOr(p.error, 1u);
+  // Row maxima and the merged denominator.
   for (int row = warp; row < rows; row += WARPS) {
     float M = -INFINITY;
-    for (int c = lane; c < cph; c += 32) M = fmaxf(M, s_w[row * cph + c]);
+    for (int c = lane; c < cph; c += 32) M = fmaxf(M, s_ml[c * (mls / 2) + row].x);
 #pragma unroll
     for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float L = 0.f;
     for (int c = lane; c < cph; c += 32) {
-      const float m = s_w[row * cph + c];
-      const float wt = (m == -INFINITY) ? 0.f : ex2(m - M);
-      s_w[row * cph + c] = wt;
-      L += wt * s_l[row * cph + c];
+      const float2 ml = s_ml[c * (mls / 2) + row];
+      L += (ml.x == -INFINITY) ? 0.f : ex2(ml.x - M) * ml.y;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
@@ -528,46 +556,54 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     }
   }
   __syncthreads();
-  constexpr int D4 = D / 4;
-  const size_t rstride = size_t(rows) * D4;   // float4s per CTA record
-  for (int idx = tid; idx < rows * D4; idx += THREADS) {
-    const int row = idx / D4, d4 = idx % D4;
-    const float4 *src = reinterpret_cast<const float4 *>(p.rec) + size_t(c0) * rstride + row * D4 + d4;
-    const float *wr = s_w + row * cph;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int c = 0;
-    for (; c + 16 <= cph; c += 16) {
-      float4 v[16];
+  // Thread tid owns the output float4s tid and tid + THREADS (at most 16
+  // rows x 64 float4s in all).
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  for (int cb = 0, chunk = 0; cb < cph; cb += mrec, ++chunk) {
+    const int cnt = min(mrec, cph - cb);
+    if (chunk > 0) {
+      __syncthreads();   // the previous chunk is consumed
+      if (tid == 0) issue(cb, cnt, false);
+      if (!mbar_wait(mbar, chunk & 1)) atomicOr(p.error, 1u);
+    }
 #pragma unroll
-      for (int k = 0; k < 16; ++k) v[k] = __ldcg(src + (c + k) * rstride);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float wt = wr[c + k];
-        acc.x += wt * v[k].x; acc.y += wt * v[k].y; acc.z += wt * v[k].z; acc.w += wt * v[k].w;
+    for (int k = 0; k < 2; ++k) {
+      const int o = tid + k * THREADS;
+      if (o < outs) {
+        const int row = o / D4;
+        const float M = s_row[2 * row];
+        const float4 *src = s_rec + o;
+        for (int c = 0; c < cnt; ++c) {
+          const float m = s_ml[(cb + c) * (mls / 2) + row].x;
+          const float wt = (m == -INFINITY) ? 0.f : ex2(m - M);
+          const float4 v = src[size_t(c) * outs];
+          acc[k].x += wt * v.x; acc[k].y += wt * v.y; acc[k].z += wt * v.z; acc[k].w += wt * v.w;
+        }
       }
     }
-    for (; c < cph; ++c) {
-      const float4 v = __ldcg(src + c * rstride);
-      const float wt = wr[c];
-      acc.x += wt * v.x; acc.y += wt * v.y; acc.z += wt * v.z; acc.w += wt * v.w;
-    }
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int o = tid + k * THREADS;
+    if (o >= outs) continue;
+    const int row = o / D4, d4 = o % D4;
     const float M = s_row[2 * row], L = s_row[2 * row + 1];
     const int nn = row / G, g = row % G;
     const int64_t orow = int64_t(head * G + g) * nq + nn;
     if (p.partial) {
-      float *o = static_cast<float *>(sd.out) + orow * (D + 2);
-      o[4 * d4] = acc.x; o[4 * d4 + 1] = acc.y; o[4 * d4 + 2] = acc.z; o[4 * d4 + 3] = acc.w;
+      float *out = static_cast<float *>(sd.out) + orow * (D + 2);
+      out[4 * d4] = acc[k].x; out[4 * d4 + 1] = acc[k].y; out[4 * d4 + 2] = acc[k].z; out[4 * d4 + 3] = acc[k].w;
       if (d4 == 0) {
-        o[D] = M;
-        o[D + 1] = L;
+        out[D] = M;
+        out[D + 1] = L;
       }
     } else {
-      T *o = static_cast<T *>(sd.out) + orow * D + 4 * d4;
+      T *out = static_cast<T *>(sd.out) + orow * D + 4 * d4;
       const float inv = 1.f / L;
-      o[0] = Elem<DT>::from_f32(acc.x * inv);
-      o[1] = Elem<DT>::from_f32(acc.y * inv);
-      o[2] = Elem<DT>::from_f32(acc.z * inv);
-      o[3] = Elem<DT>::from_f32(acc.w * inv);
+      out[0] = Elem<DT>::from_f32(acc[k].x * inv);
+      out[1] = Elem<DT>::from_f32(acc[k].y * inv);
+      out[2] = Elem<DT>::from_f32(acc[k].z * inv);
+      out[3] = Elem<DT>::from_f32(acc[k].w * inv);
     }
   }
   if (tid == 0) p.counters[seq * p.hkv + head] = 0u;
@@ -645,7 +681,7 @@ int make_plan(const ckv_attn_args &a, int D, Plan &pl) {
   pl.rows = a.nq * (a.heads_q / a.heads_kv);
   pl.rec_off = kCounterBytes;
   pl.ml_off = pl.rec_off + (size_t(grid) * pl.rows * D * 4 + 255) / 256 * 256;
-  pl.bytes = pl.ml_off + (size_t(grid) * pl.rows * 2 * 4 + 255) / 256 * 256;
+  pl.bytes = pl.ml_off + (size_t(grid) * ml_stride(pl.rows) * 4 + 255) / 256 * 256;
   return CKV_OK;
 }
 

@@ -89,7 +89,7 @@ struct ParamsHead {
   int32_t partial;
   float scale_log2;
   float *rec;           // [grid][rows][D]
-  float *rec_ml;        // [grid][rows][2]
+  float *rec_ml;        // [grid][ml_stride(rows)]: (m, l) per row
   unsigned *counters;   // [num_seqs * hkv]
   unsigned *error;      // set to 1 when a wait gives up
 };
@@ -104,6 +104,9 @@ struct alignas(64) Params : ParamsHead {
 constexpr int kMaxCph = 256;  // CTAs per (sequence, KV head), bounded by the merge scratch
 
 constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
+// Floats per CTA in the (m, l) record array: two per row, padded to 16 bytes
+// so that the records of consecutive CTAs form one bulk copy.
+__host__ __device__ constexpr int ml_stride(int rows) { return (rows * 2 + 3) & ~3; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 template <int BITS, int D, int NT>
@@ -145,7 +148,9 @@ struct Cfg {
   // End-of-CTA scratch (reuses the stage rings).
   static constexpr int RED = TEAMS * ROWS * D * 4;                 // [team][ROWS][D]
   static_assert(RED + 64 * ROWS * 4 <= NK * KST + NV * VST, "reduction scratch");
-  static_assert(16 * kMaxCph * 2 * 4 + 16 * 2 * 4 <= NK * KST + NV * VST, "merge scratch");
+  // Merge scratch: the (m, l) records, the rows' (M, L), then at least one record.
+  static_assert(kMaxCph * ml_stride(ROWS) * 4 + 2 * ROWS * 4 + 128 + ROWS * D * 4 <= NK * KST + NV * VST,
+                "merge scratch");
 };
 
 // Offset of byte `a` of a TMA box (rows of 128/64/32 bytes) after the hardware
