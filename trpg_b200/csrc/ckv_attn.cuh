@@ -101,7 +101,7 @@ struct alignas(64) Params : ParamsHead {
   SeqDev seq[MAXS];
 };
 
-constexpr int kMaxCph = 256;  // CTAs per (sequence, KV head), bounded by the merge scratch
+constexpr int kMaxCph = 160;  // CTAs per (sequence, KV head): one wave of SMs, bounded by the merge scratch
 
 constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
 // Floats per CTA in the (m, l) record array: two per row, padded to 16 bytes
@@ -148,8 +148,11 @@ struct Cfg {
   // End-of-CTA scratch (reuses the stage rings).
   static constexpr int RED = TEAMS * ROWS * D * 4;                 // [team][ROWS][D]
   static_assert(RED + 64 * ROWS * 4 <= NK * KST + NV * VST, "reduction scratch");
-  // Merge scratch: the (m, l) records, the rows' (M, L), then at least one record.
-  static_assert(kMaxCph * ml_stride(ROWS) * 4 + 2 * ROWS * 4 + 128 + ROWS * D * 4 <= NK * KST + NV * VST,
+  // Merge scratch: (m, l) records, weights, the rows' (M, L), the partial
+  // sums of the record parts, then at least one record.
+  static_assert(kMaxCph * (ml_stride(ROWS) + ROWS) * 4 + 2 * ROWS * 4 + 16 + THREADS * 16 + 128 +
+                        ROWS * D * 4 <=
+                    NK * KST + NV * VST,
                 "merge scratch");
 };
 
