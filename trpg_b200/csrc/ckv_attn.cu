@@ -491,13 +491,16 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();   // the whole CTA's record stores (ordered by the barrier) before the ticket
-    const unsigned prev = atomicAdd(&p.counters[seq * p.hkv + head], 1u);
-    const bool last = prev == unsigned(sd.cph - 1);
-    // Acquire side: the other CTAs' records (released by their fences before
-    // their tickets) are visible to every thread ordered after the barrier.
-    if (last) __threadfence();
-    s_last = last;
+    // Release: the whole CTA's record stores (ordered before this thread by
+    // the barrier) become visible with the ticket.  Acquire: for the last
+    // CTA, the other CTAs' records are visible to every thread ordered after
+    // the next barrier.
+    unsigned prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                 : "=r"(prev)
+                 : "l"(&p.counters[seq * p.hkv + head])
+                 : "memory");
+    s_last = prev == unsigned(sd.cph - 1);
   }
   __syncthreads();
   if (!s_last) return;
