@@ -692,14 +692,19 @@ int seq_items(const ckv_seq &s) {
 constexpr int kItemsPerCta = 8;   // items (blocks / residual chunks) one CTA pipelines
 
 // CTAs per (sequence, KV head): a whole number of waves of one CTA per SM,
-// about kItemsPerCta items per CTA, shared out in proportion to each pair's
-// items.
+// shared out in proportion to each pair's items.
 int make_plan(const ckv_attn_args &a, int D, Plan &pl) {
   const int sms = sm_count();
   int64_t total = 0;
   for (int i = 0; i < a.num_seqs; ++i) total += int64_t(seq_items(a.seqs[i])) * a.heads_kv;
   const int64_t per_wave = int64_t(sms) * kItemsPerCta;
-  const int64_t waves = std::max<int64_t>(1, (total + per_wave - 1) / per_wave);
+  // Few pairs (each gets at least 8 CTAs of one wave): one wave, however long
+  // the ranges -- no wave tails and fewer records to merge.  Many pairs:
+  // whole waves of about kItemsPerCta items, which the block scheduler
+  // balances across ragged pairs.
+  const int64_t pairs = int64_t(a.num_seqs) * a.heads_kv;
+  const int64_t waves =
+      pairs * 8 <= sms ? 1 : std::max<int64_t>(1, (total + per_wave - 1) / per_wave);
   const int64_t target = int64_t(sms) * waves;
   int grid = 0;
   for (int i = 0; i < a.num_seqs; ++i) {

@@ -189,6 +189,21 @@ __device__ __forceinline__ float pow2i(float d) {
   return !(d >= -126.f) ? 0.f : __int_as_float((int(d) + 127) << 23);
 }
 
+// Nibble K (bits [4K, 4K + 4), K < 5) of w as the exact float 2^(23-4K) + code:
+// the nibble lands in the mantissa bits whose weights are 2^0..2^3 under
+// that exponent, so one and-or forms it.
+template <int K>
+__device__ __forceinline__ float nib_magic(uint32_t w) {
+  static_assert(K >= 0 && K < 5, "nibble above the mantissa");
+  return __uint_as_float((w & (0xFu << (4 * K))) | (uint32_t(127 + 23 - 4 * K) << 23));
+}
+// (-2^(23-4K), -2^(19-4K)): takes the offsets of nibbles K and K + 1 away.
+template <int K>
+__device__ __forceinline__ float2 nib_bias() {
+  return make_float2(-__uint_as_float(uint32_t(127 + 23 - 4 * K) << 23),
+                     -__uint_as_float(uint32_t(127 + 19 - 4 * K) << 23));
+}
+
 // Two codes held as 2^23 + code -> fma(code, scale, low) in fp32.
 __device__ __forceinline__ float2 dq2(float2 magic, float sc, float lo) {
   const float2 c = __fadd2_rn(magic, make_float2(-kMagic, -kMagic));
@@ -257,15 +272,20 @@ struct QkWarp {
           x0 = make_float2(byte_magic<0>(w), byte_magic<1>(w));
           x1 = make_float2(byte_magic<2>(w), byte_magic<3>(w));
         } else {
-          // two bytes: tokens 4r+0 (low nibble), +1 (high), +2, +3
+          // two bytes: tokens 4r+0 (low nibble), +1 (high), +2, +3; nibble k
+          // becomes 2^(23-4k) + code with one logic op (nib_magic).
           const uint32_t w = *reinterpret_cast<const uint16_t *>(src);
-          const uint32_t lo4 = w & 0x0F0Fu, hi4 = (w >> 4) & 0x0F0Fu;
-          x0 = make_float2(byte_magic<0>(lo4), byte_magic<0>(hi4));
-          x1 = make_float2(byte_magic<1>(lo4), byte_magic<1>(hi4));
+          x0 = make_float2(nib_magic<0>(w), nib_magic<1>(w));
+          x1 = make_float2(nib_magic<2>(w), nib_magic<3>(w));
         }
         const float2 sc2 = make_float2(sc[e], sc[e]), lo2 = make_float2(lo[e], lo[e]);
-        x0 = dq2p(x0, sc2, lo2);
-        x1 = dq2p(x1, sc2, lo2);
+        if constexpr (BITS == 8) {
+          x0 = dq2p(x0, sc2, lo2);
+          x1 = dq2p(x1, sc2, lo2);
+        } else {
+          x0 = __ffma2_rn(__fadd2_rn(x0, nib_bias<0>()), sc2, lo2);
+          x1 = __ffma2_rn(__fadd2_rn(x1, nib_bias<2>()), sc2, lo2);
+        }
         f[e][0] = x0.x; f[e][1] = x0.y; f[e][2] = x1.x; f[e][3] = x1.y;
       }
       uint2 b[NT];
