@@ -706,14 +706,36 @@ int make_plan(const ckv_attn_args &a, int D, Plan &pl) {
   const int64_t waves =
       pairs * 8 <= sms ? 1 : std::max<int64_t>(1, (total + per_wave - 1) / per_wave);
   const int64_t target = int64_t(sms) * waves;
-  int grid = 0;
+  // Largest remainders: the pairs' CTA counts add up to the target grid
+  // exactly (whole waves), each count within [1, min(items, kMaxCph)].
+  int64_t rem[CKV_MAX_SEQS];
+  int64_t used = 0;
   for (int i = 0; i < a.num_seqs; ++i) {
     const int items = seq_items(a.seqs[i]);
-    int64_t c = total > 0 ? (target * items + total / 2) / total : 1;
-    c = std::max<int64_t>(1, std::min<int64_t>({c, std::max(items, 1), int64_t(kMaxCph)}));
+    const int64_t cap = std::min<int64_t>(std::max(items, 1), kMaxCph);
+    const int64_t num = total > 0 ? target * items : 0;
+    int64_t c = total > 0 ? num / total : 1;
+    rem[i] = total > 0 ? num % total : 0;
+    c = std::max<int64_t>(1, std::min<int64_t>(c, cap));
+    if (c == cap) rem[i] = -1;
     pl.cph[i] = int(c);
+    used += c * a.heads_kv;
+  }
+  // Hand out whole CTA-per-pair increments (heads_kv CTAs each) by remainder.
+  while (used + a.heads_kv <= target) {
+    int best = -1;
+    for (int i = 0; i < a.num_seqs; ++i)
+      if (rem[i] >= 0 && (best < 0 || rem[i] > rem[best])) best = i;
+    if (best < 0) break;
+    ++pl.cph[best];
+    used += a.heads_kv;
+    const int items = seq_items(a.seqs[best]);
+    rem[best] = pl.cph[best] >= std::min<int64_t>(std::max(items, 1), kMaxCph) ? -1 : 0;
+  }
+  int grid = 0;
+  for (int i = 0; i < a.num_seqs; ++i) {
     pl.cta_begin[i] = grid;
-    grid += int(c) * a.heads_kv;
+    grid += pl.cph[i] * a.heads_kv;
   }
   pl.grid = grid;
   pl.rows = a.nq * (a.heads_q / a.heads_kv);
