@@ -177,8 +177,10 @@ Tensor fit_rows(const Tensor &t) {
 
 // keys[:, :, offset:offset+n] = keys_new (and values) for window buffers
 // [1,H,C,D] with capacity C >= offset + n; one launch.
-void residual_append(const Tensor &keys_new, const Tensor &values_new, const Tensor &keys,
-                     const Tensor &values, int64_t offset) {
+// Writes the new rows at `offset` and returns the window views of the rows
+// written so far (the first offset + n rows of each buffer).
+std::tuple<Tensor, Tensor> residual_append(const Tensor &keys_new, const Tensor &values_new,
+                                           const Tensor &keys, const Tensor &values, int64_t offset) {
   for (auto *t : {&keys_new, &values_new, &keys, &values}) require_cuda(*t, "residual tensor");
   TORCH_CHECK(keys_new.dim() == 4 && values_new.sizes() == keys_new.sizes() && keys_new.size(0) == 1,
               "ckv::residual_append: new rows must be [1,H,n,D]");
@@ -215,6 +217,8 @@ void residual_append(const Tensor &keys_new, const Tensor &values_new, const Ten
                   values.stride(2) % 8 == 0,
               "ckv::residual_append: window buffers need dense, 16-byte aligned rows");
   check_status(ckv_residual_append(&a, current_stream(keys)), "residual_append");
+  const int64_t rows = offset + keys_new.size(2);
+  return {keys.narrow(2, 0, rows), values.narrow(2, 0, rows)};
 }
 
 // ---------------------------------------------------------------------------
@@ -474,7 +478,7 @@ TORCH_LIBRARY(ckv, m) {
       "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
   m.def("attention_error(Tensor like) -> int");
   m.def("residual_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
-        "int offset) -> ()");
+        "int offset) -> (Tensor(a), Tensor(b))");
 }
 
 namespace {

@@ -47,13 +47,18 @@ VALUE_SLAB_TOKENS = 4096  # models/quantized_kv.py:51
 _residual_append_op = None
 
 
-def _residual_append(keys_new, values_new, kb, vb, offset):
-    """One launch writes the new key and value rows into the window buffers
-    (the op copies rows it cannot read directly)."""
+def _residual_op():
     global _residual_append_op
     if _residual_append_op is None:
         _residual_append_op = ops().residual_append
-    _residual_append_op(keys_new, values_new, kb, vb, offset)
+    return _residual_append_op
+
+
+def _residual_append(keys_new, values_new, kb, vb, offset):
+    """One launch writes the new key and value rows into the window buffers
+    (the op copies rows it cannot read directly); returns the window views of
+    the first offset + n rows."""
+    return _residual_op()(keys_new, values_new, kb, vb, offset)
 
 
 def _pack(rows, bits, rounding=None):
@@ -163,12 +168,14 @@ class QuantizedAttentionLayer(DynamicLayer):
             # Fast path: keys / values are the views this layer made last time
             # (the op checks dtype and device).
             r = w[4]
-            _residual_append(key_states, value_states, w[0], w[1], r)
-            self._set_window(w[0], w[1], r + n)
+            keys, values = (_residual_append_op or _residual_op())(key_states, value_states,
+                                                                   w[0], w[1], r)
+            self.keys, self.values = keys, values
+            self._window = (w[0], w[1], keys, values, r + n, w[5])
             self.cumulative_length += n
-            return QuantizedKVView(self.key_bank.data, self.key_bank.meta, self.value_bank.data,
-                                   self.value_bank.meta, self.key_bank.units * 128, self.keys,
-                                   self.values, self.bits, self.cumulative_length)
+            kb, vb = self.key_bank, self.value_bank
+            return QuantizedKVView(kb.data, kb.meta, vb.data, vb.meta, kb.units * 128, keys, values,
+                                   self.bits, self.cumulative_length)
         if key_states.shape[-1] % 64 or value_states.shape[-1] % 64:
             raise ValueError('quantized KV needs head_dim to be a multiple of 64')
         if not self.is_initialized:
@@ -183,8 +190,8 @@ class QuantizedAttentionLayer(DynamicLayer):
         else:
             kb, vb = self._window_for(key_states, n)
             r = self.keys.shape[-2] if self.keys.dim() == 4 else 0
-            _residual_append(key_states, value_states, kb, vb, r)
-            self._set_window(kb, vb, r + n)
+            self.keys, self.values = _residual_append(key_states, value_states, kb, vb, r)
+            self._window = (kb, vb, self.keys, self.values, r + n, kb.shape[2])
         return QuantizedKVView(self.key_bank.data, self.key_bank.meta,
                                self.value_bank.data, self.value_bank.meta,
                                self.key_bank.units * 128, self.keys, self.values,
