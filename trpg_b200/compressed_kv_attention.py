@@ -52,17 +52,25 @@ def _query_ok(query, scale):
             and math.isfinite(scale))
 
 
+_guarded_op = None
+
+
 def compressed_kv_decode(query, view, scale):
-    """Single-query decode, or None when unsupported (reference ``:8-29``)."""
-    if not _query_ok(query, scale) or query.shape[2] != 1 or view.packed_tokens < 128:
+    """Single-query decode, or None when unsupported (reference ``:8-29``).
+
+    One op call (``torch.ops.ckv.decode_guarded``) applies the guard of
+    ``_query_ok`` / ``_view_ok`` in C++ and runs the kernel when it passes.
+    """
+    global _guarded_op
+    length, bits, packed = view.length, view.bits, view.packed_tokens
+    if (type(length) is not int or type(packed) is not int or type(bits) is not int
+            or not isinstance(scale, (int, float)) or isinstance(scale, bool)):
         return None
-    if not _view_ok(query, view, 0) or query.shape[1] // view.keys.shape[1] > 16:
-        return None
-    try:
-        from .compressed_kv_kernels import decode
-    except ImportError:
-        return None
-    return decode(query, view, scale)
+    if _guarded_op is None:
+        from ._native import ops
+        _guarded_op = ops().decode_guarded
+    return _guarded_op(query, view.key_data, view.key_meta, view.value_data, view.value_meta,
+                       view.keys, view.values, packed, length, bits, float(scale))
 
 
 def compressed_kv_verify(query, view, scale):

@@ -4,6 +4,7 @@
 // picks the current CUDA stream and calls the C ABI of libtrpg_ckv.so.  No
 // computation happens here and there is no CPU implementation.
 #include <ATen/ATen.h>
+#include <ATen/autocast_mode.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
@@ -420,6 +421,38 @@ Tensor decode(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor 
   return out;
 }
 
+// compressed_kv_decode's guard (models/compressed_kv_attention.py:8-29), in
+// one call: nullopt for anything the kernel does not cover (the caller then
+// falls back to SDPA), else decode's output.  The checks match
+// trpg_b200.compressed_kv_attention._query_ok / _view_ok.
+std::optional<Tensor> decode_guarded(const Tensor &q, const std::optional<Tensor> &kd,
+                                     const std::optional<Tensor> &km,
+                                     const std::optional<Tensor> &vd,
+                                     const std::optional<Tensor> &vm,
+                                     const std::optional<Tensor> &rk,
+                                     const std::optional<Tensor> &rv, int64_t packed,
+                                     int64_t length, int64_t bits, double scale) {
+  if (!q.is_cuda() || at::GradMode::is_enabled() || at::autocast::is_autocast_enabled(at::kCUDA))
+    return std::nullopt;
+  if (q.dim() != 4 || q.size(0) != 1 || q.size(2) != 1 || q.requires_grad() || q.stride(3) != 1)
+    return std::nullopt;
+  const auto dt = q.scalar_type();
+  const int64_t d = q.size(3);
+  if ((dt != at::kBFloat16 && dt != at::kHalf) || (d != 64 && d != 128 && d != 256) ||
+      !std::isfinite(scale) || (bits != 4 && bits != 8) || packed < 128)
+    return std::nullopt;
+  for (const auto *t : {&kd, &km, &vd, &vm, &rk, &rv})
+    if (!t->has_value() || !(*t)->defined() || (*t)->device() != q.device() || (*t)->requires_grad())
+      return std::nullopt;
+  const Tensor &keys = *rk, &values = *rv;
+  if (keys.dim() != 4 || values.sizes() != keys.sizes() || keys.size(0) != 1 ||
+      keys.scalar_type() != dt || values.scalar_type() != dt || keys.size(3) != d ||
+      q.size(1) % keys.size(1) != 0 || q.size(1) / keys.size(1) > 16 ||
+      length != packed + keys.size(2) || keys.stride(3) != 1 || values.stride(3) != 1)
+    return std::nullopt;
+  return decode(q, *kd, *km, *vd, *vm, keys, values, packed, length, bits, scale);
+}
+
 Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
   require_cuda(partials, "partials");
   TORCH_CHECK(partials.dim() == 3 && partials.scalar_type() == at::kFloat,
@@ -477,6 +510,12 @@ TORCH_LIBRARY(ckv, m) {
       "decode(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
       "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
   m.def("attention_error(Tensor like) -> int");
+  // Any device (a CPU query gets None), so a catch-all kernel.
+  m.def(
+      "decode_guarded(Tensor query, Tensor? key_data, Tensor? key_meta, Tensor? value_data, "
+      "Tensor? value_meta, Tensor? keys, Tensor? values, int packed, int length, int bits, "
+      "float scale) -> Tensor?",
+      &decode_guarded);
   m.def("residual_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
         "int offset) -> (Tensor(a), Tensor(b))");
 }
