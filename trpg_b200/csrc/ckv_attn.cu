@@ -115,10 +115,20 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const int ni = np + nr;
   const int ib = int(int64_t(rsplit) * ni / sd.cph);
   const int n = int(int64_t(rsplit + 1) * ni / sd.cph) - ib;
+  // Local order of the range: its first packed block (issued before the
+  // wait on the previous kernel), then its exact-window chunks (loaded only
+  // after that wait, so they get the whole pipeline to arrive), then the
+  // other packed blocks.  item(i) is the range's item at local position i.
+  const int npk = max(0, min(n, np - ib));       // packed blocks in the range
+  const int nrs = n - npk;                       // window chunks in the range
+  auto item = [&](int i) {
+    if (npk == 0 || nrs == 0 || i == 0) return ib + i;
+    return i <= nrs ? ib + npk + (i - 1) : ib + (i - nrs);
+  };
 
   // Producer side of one packed item: stage st of the K (kchain) or V ring.
   auto issue_packed = [&](bool kchain, int i, int st) {
-    const int unit = sd.ub + ib + i;
+    const int unit = sd.ub + item(i);
     if (kchain) {
       const uint32_t dst = sbase + C::OFF_K + st * C::KST, fb = bar(KFULL + st);
       mbar_expect_tx(fb, C::KCODE + C::KMETA);
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       }
       if (!__shfl_sync(0xffffffffu, go, 0)) break;
       const uint32_t dst = ring + st * stage_bytes, fb = bar(full0 + st);
-      const int it = ib + i;
+      const int it = item(i);
       if (it < np) {
         if (lane == 0) issue_packed(kchain, i, st);
       } else {
@@ -254,7 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     for (int i = team; i < n; i += TEAMS) {
       const int k = i >> 1, par = k & 1;
       const int st = i % NK;
-      const int it = ib + i;
+      const int it = item(i);
       const bool pk = it < np;
       float S[2][NT][4];
       const bool have = !s_abort && wait_stage(bar(KFULL + st), &s_issued[st], i, i / NK, &s_abort);
@@ -351,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     for (int i = team; i < n; i += TEAMS) {
       const int k = i >> 1, par = k & 1;
       const int sv = i % NV;
-      const bool pk = ib + i < np;
+      const bool pk = item(i) < np;
       bool ok = !s_abort && wait_stage(bar(VFULL + sv), &s_issued[NK + sv], i, i / NV, &s_abort);
       ok = ok && wait_or_abort(bar(PFULL + team * 2 + par), (k >> 1) & 1, &s_abort);
       if (!ok && !s_abort) fail();
