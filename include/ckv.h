@@ -235,6 +235,34 @@ static inline int64_t ckv_partial_row(int hq, int n, int nq) { return (int64_t)h
 int ckv_combine_partials(const float *partials, int parts, int64_t rows, int head_dim,
                          int dtype, void *out, ckv_stream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Packed prefill                                                          */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Lower-right causal attention of a query chunk over the whole quantized
+ * history plus the exact residual window, which already holds the chunk
+ * (the caller appends before and compacts after).  Replaces the kernel
+ * behind models/compressed_prefill_attention.py:6-52
+ * (models/compressed_prefill_kernels.py:29-111).
+ *
+ * seq:   query [Hq,qlen,D] (q_stride_head, q_stride_pos multiples of 8, base
+ *        16-byte aligned), the banks as for ckv_attention, the residual
+ *        [Hkv,R,D] (strides multiples of 8, bases 16-byte aligned) and out
+ *        [Hq,qlen,D] dense.  The ranges must cover the whole history:
+ *        unit_begin = 0, unit_end = P/128, resid_begin = 0, resid_end = R.
+ * Needs P >= 128 and R >= qlen.  Residual token t is visible to query
+ * position n iff t <= R - qlen + n; every packed token is visible.
+ * Scratch-free: one launch, no workspace.
+ */
+typedef struct {
+  ckv_seq seq;
+  int32_t heads_q, heads_kv, head_dim, qlen, bits, dtype;
+  float scale;                  /* softmax scale applied to q.k */
+} ckv_prefill_args;
+
+int ckv_prefill(const ckv_prefill_args *args, ckv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,7 +56,7 @@ def test_torch_ops_register_without_cuda():
     _native.load()
     import torch
     for op in ('pack_rows', 'unpack_rows', 'pack_append', 'attention', 'combine_partials', 'decode',
-               'attention_error'):
+               'attention_error', 'prefill'):
         assert hasattr(torch.ops.ckv, op)
 
 

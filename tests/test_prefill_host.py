@@ -1,0 +1,70 @@
+"""Packed prefill on the host: the public guard's CPU behaviour
+(tests/test_compressed_prefill_attention.py:11-19) and the C ABI's argument
+checks, which return before any CUDA call (these run without a GPU)."""
+import ctypes
+import sys
+from unittest.mock import patch
+
+import torch
+
+from trpg_b200 import _native
+
+from tests.test_zz_no_alloc import Seq
+
+I32 = ctypes.c_int32
+P, R, QLEN, D = 256, 48, 32, 64
+
+
+class PrefillArgs(ctypes.Structure):
+    """``ckv_prefill_args`` of include/ckv.h."""
+    _fields_ = [('seq', Seq), ('heads_q', I32), ('heads_kv', I32), ('head_dim', I32),
+                ('qlen', I32), ('bits', I32), ('dtype', I32), ('scale', ctypes.c_float)]
+
+
+def _lib():
+    lib = _native.library()
+    lib.ckv_prefill.argtypes = [ctypes.POINTER(PrefillArgs), ctypes.c_void_p]
+    lib.ckv_prefill.restype = ctypes.c_int
+    return lib
+
+
+def _args(**over):
+    base = 0x10000000          # fake, aligned; validation reads no memory
+    seq = Seq(base, QLEN * D, D, base, 2 * D * 128, D * 128, base, 2 * D * 2, D * 2,
+              base, 512 * D, D, base, 512 * 2, 2, base, R * D, D, base, R * D, D,
+              P, P + R, 0, P // 128, 0, R, base)
+    for k, v in over.items():
+        if hasattr(seq, k):
+            setattr(seq, k, v)
+    a = PrefillArgs(seq, 4, 2, D, QLEN, 8, 0, .125)
+    for k, v in over.items():
+        if k in dict(PrefillArgs._fields_):
+            setattr(a, k, v)
+    return a
+
+
+def test_cpu_query_never_imports_or_launches_the_kernel():
+    from trpg_b200.compressed_prefill_attention import compressed_kv_prefill
+    from trpg_b200.quantized_kv import QuantizedKVView
+    x = torch.randn(1, 1, 256, 64)
+    view = QuantizedKVView(None, None, None, None, 128, x, x, 4, 384)
+    with torch.inference_mode(), patch.dict(sys.modules, {'trpg_b200.compressed_prefill_kernels': None}):
+        assert compressed_kv_prefill(x[:, :, :16], view, .125) is None
+
+
+def test_prefill_rejects_bad_arguments_before_any_launch():
+    lib = _lib()
+    assert lib.ckv_prefill(None, None) == 1
+    bad = {
+        'qlen': R + 1,                 # the window must hold the chunk
+        'packed_tokens': 0,            # needs packed history
+        'bits': 5,
+        'heads_q': 3,                  # not a multiple of heads_kv
+        'scale': float('nan'),
+        'q_stride_pos': D + 4,         # rows not 16-byte aligned
+        'keys': 0x10000008,            # residual base not 16-byte aligned
+    }
+    for k, v in bad.items():
+        assert lib.ckv_prefill(ctypes.byref(_args(**{k: v})), None) == 1, k
+    assert lib.ckv_prefill(ctypes.byref(_args(head_dim=96)), None) == 2
+    assert lib.ckv_prefill(ctypes.byref(_args(resid_begin=8)), None) == 2   # a shard

@@ -453,6 +453,39 @@ std::optional<Tensor> decode_guarded(const Tensor &q, const std::optional<Tensor
   return decode(q, *kd, *km, *vd, *vm, keys, values, packed, length, bits, scale);
 }
 
+// Packed prefill over one sequence's whole history
+// (models/compressed_prefill_kernels.py:98-111): out [1,Hq,qlen,D] dense.
+Tensor prefill(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor &vd,
+               const Tensor &vm, const Tensor &rk, const Tensor &rv, int64_t packed,
+               int64_t length, int64_t bits, double scale) {
+  require_cuda(q, "query");
+  TORCH_CHECK(q.dim() == 4 && q.size(0) == 1 && q.stride(3) == 1,
+              "ckv::prefill: query must be [1,Hq,qlen,D] with a dense last dim");
+  for (const Tensor *t : {&kd, &km, &vd, &vm, &rk, &rv})
+    TORCH_CHECK(t->defined() && t->device() == q.device(),
+                "ckv::prefill: all tensors must be on the query's device");
+  TORCH_CHECK(packed >= 128 && packed % 128 == 0, "ckv::prefill: packed must be a positive multiple of 128");
+  c10::cuda::CUDAGuard guard(q.device());
+  const int64_t range[4] = {0, packed / 128, 0, rk.size(2)};
+  const int64_t hkv = rk.size(1);
+  const Tensor q2 = fit_rows(q);
+  const Tensor kd2 = fit_bank(kd, 2), km2 = fit_bank(km, 2), vd2 = fit_bank(vd, 3),
+               vm2 = fit_bank(vm, 3), rk2 = fit_rows(rk), rv2 = fit_rows(rv);
+  ckv_prefill_args a{};
+  a.seq = make_seq(q2, kd2, km2, vd2, vm2, rk2, rv2, packed, length, range, bits, hkv);
+  Tensor out = at::empty(q.sizes(), q.options().memory_format(at::MemoryFormat::Contiguous));
+  a.seq.out = out.data_ptr();
+  a.heads_q = int32_t(q.size(1));
+  a.heads_kv = int32_t(hkv);
+  a.head_dim = int32_t(q.size(3));
+  a.qlen = int32_t(q.size(2));
+  a.bits = int32_t(bits);
+  a.dtype = dtype_code(q.scalar_type());
+  a.scale = float(scale);
+  check_status(ckv_prefill(&a, current_stream(q)), "prefill");
+  return out;
+}
+
 Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
   require_cuda(partials, "partials");
   TORCH_CHECK(partials.dim() == 3 && partials.scalar_type() == at::kFloat,
@@ -510,6 +543,9 @@ TORCH_LIBRARY(ckv, m) {
       "decode(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
       "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
   m.def("attention_error(Tensor like) -> int");
+  m.def(
+      "prefill(Tensor query, Tensor key_data, Tensor key_meta, Tensor value_data, Tensor value_meta, "
+      "Tensor keys, Tensor values, int packed, int length, int bits, float scale) -> Tensor");
   // Any device (a CPU query gets None), so a catch-all kernel.
   m.def(
       "decode_guarded(Tensor query, Tensor? key_data, Tensor? key_meta, Tensor? value_data, "
@@ -554,4 +590,5 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("decode", &decode);
   m.impl("attention_error", &attention_error);
   m.impl("residual_append", &residual_append);
+  m.impl("prefill", &prefill);
 }
