@@ -441,6 +441,9 @@ WORKLOADS = {
           '16q/4kv x 256, one launch per GPU; sequences sharded over GPUs',
     'c5': 'long-context Q4 decode: 1 sequence, 131072 context, 16q/4kv x 256; split-KV over GPUs, '
           '(m, l, o) partials all-gathered over NCCL and merged',
+    'prefill': 'packed prefill: one query chunk (--qlen, default 4096) over a quantized history '
+               '(--history, default 32768; --bits, default 8), 16q/4kv x 256, lower-right causal; '
+               'replicas only across GPUs',
 }
 
 
@@ -581,6 +584,62 @@ def extra_workload(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def prefill_workload(args, world, rank, local):
+    """Packed prefill (``compressed_kv_prefill``) against dequantize + SDPA on
+    the same view, both device-timed from CUDA-graph replays: the shapes of
+    the reference's prefill profile (scripts/profile_compressed_prefill.py:36-47)."""
+    from torch.nn.attention.bias import causal_lower_right
+    from torch.nn import functional as F
+    from trpg_b200 import _native
+    from trpg_b200.compressed_prefill_attention import compressed_kv_prefill
+    _native.load()
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(104 + rank)
+    qlen, history, bits = args.qlen, args.history, args.bits
+    layer, view = build_view(gen, history + qlen, qlen, bits, device)
+    q = torch.randn(1, qlen, HQ, D, generator=gen, device=device).bfloat16().transpose(1, 2)
+    bias = causal_lower_right(qlen, view.length)
+
+    def packed():
+        out = compressed_kv_prefill(q, view, SCALE)
+        assert out is not None
+        return out
+
+    def unpack_sdpa():
+        keys = torch.cat((layer.key_bank.unpack(q.dtype), view.keys), -2)
+        values = torch.cat((layer.value_bank.unpack(q.dtype), view.values), -2)
+        return F.scaled_dot_product_attention(q, keys, values, attn_mask=bias, enable_gqa=True,
+                                              scale=SCALE)
+
+    with torch.inference_mode():
+        err = (packed().float() - unpack_sdpa().float()).abs().max().item()
+    clocks = Clocks(local)
+    clocks.start()
+    sec = max_over_ranks(graph_seconds(packed, replays=max(3, args.steps)), world)
+    clocks.stop()
+    sec_ref = max_over_ranks(graph_seconds(unpack_sdpa, replays=max(3, args.steps)), world)
+    P, R = view.packed_tokens, view.keys.shape[2]
+    visible = qlen * P + qlen * (R - qlen) + qlen * (qlen + 1) // 2
+    flops = 4 * HQ * D * visible
+    path = ROOT / 'MEASURED_PEAKS.json'
+    peak = json.loads(path.read_text()).get('bf16_tflops') if path.exists() else None
+    peak, kind = (float(peak), 'measured') if peak else (1590.0, 'fallback')
+    achieved = flops / sec / 1e12
+    line = {'metric': 'prefill: query tokens/s', 'workload': WORKLOADS['prefill'],
+            'value': world * qlen / sec, 'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps,
+            'higher_is_better': True, 'scaling': 'weak (replicas)', 'dtype': f'u{bits}/bf16',
+            'data': 'synthetic', 'ms_per_call': sec * 1e3, 'history': P + R - qlen, 'qlen': qlen,
+            'dequant_sdpa_ms': sec_ref * 1e3, 'speedup_vs_dequant_sdpa': sec_ref / sec,
+            'max_abs_vs_dequant_sdpa': err,
+            'roofline': {'bound': 'tensor', 'achieved': achieved, 'peak': peak, 'unit': 'TFLOP/s',
+                         'frac': achieved / peak, 'peak_source': kind, 'flops_per_launch': flops},
+            'clocks': clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -592,6 +651,9 @@ def main():
     ap.add_argument('--workload', choices=('c2',) + tuple(WORKLOADS), default='c2',
                     help='c2 (default) is the headline 32K decode step; c3/c4/c5 measure the '
                          'other configurations')
+    ap.add_argument('--history', type=int, default=32768, help='prefill: history tokens')
+    ap.add_argument('--qlen', type=int, default=4096, help='prefill: query chunk length')
+    ap.add_argument('--bits', type=int, choices=(4, 8), default=8, help='prefill: code width')
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
@@ -599,6 +661,8 @@ def main():
     try:
         if args.impl == 'reference':
             reference_arm(args, world, rank)
+        elif args.workload == 'prefill':
+            prefill_workload(args, world, rank, local)
         elif args.workload != 'c2':
             extra_workload(args, world, rank, local)
         else:

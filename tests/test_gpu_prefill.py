@@ -124,3 +124,50 @@ def test_prefill_then_decode_on_the_same_layer():
         q1 = O.seeded_normal(505, (1, 4, 1, 128))
         out = compressed_kv_decode(to_torch(q1, 'bfloat16'), dview, 128 ** -.5)
     check(out, O.decode_reference(q1, ol, 128 ** -.5))
+
+
+def test_real_qwen_attention_routes_a_prefill_chunk_and_keeps_the_cache():
+    """A second prefill chunk through the patched ``Qwen3_5Attention`` matches
+    the unpatched module (dequantize + SDPA via the cache's ``update``) and
+    leaves the same cache state (after the reference's real-attention test,
+    tests/test_compressed_kv_attention.py:159-187)."""
+    import copy
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
+    from torch.nn.attention.bias import causal_lower_right
+    from trpg_b200.compressed_kv_attention import compressed_kv_info, configure_compressed_kv_attention
+    from trpg_b200.quantized_kv import make_cache
+    torch.manual_seed(0)
+    config = Qwen3_5TextConfig(hidden_size=128, intermediate_size=256, num_hidden_layers=1,
+                               num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                               layer_types=['full_attention'])
+    config._attn_implementation = 'sdpa'
+    module = Qwen3_5Attention(config, 0).cuda().bfloat16().eval().requires_grad_(False)
+    configure_compressed_kv_attention(module, False)
+    cache = make_cache(config, 'q8')
+    n0, n1 = 384, 64
+    x = torch.randn(1, n0 + n1, 128, device='cuda', dtype=torch.bfloat16)
+    angle = torch.randn(1, n0 + n1, 64, device='cuda')
+    pos = (angle.cos().bfloat16(), angle.sin().bfloat16())
+    with torch.inference_mode():
+        module(x[:, :n0], tuple(t[:, :n0] for t in pos), causal_lower_right(n0, n0), past_key_values=cache)
+        ref, direct = copy.deepcopy(cache), copy.deepcopy(cache)
+        hidden = x[:, n0:].contiguous()
+        positions = tuple(t[:, n0:].contiguous() for t in pos)
+        mask = causal_lower_right(n1, n0 + n1)
+        expected, _ = module(hidden, positions, mask, past_key_values=ref)
+        plain = copy.deepcopy(direct)
+        configure_compressed_kv_attention(module, True)           # prefill routing off
+        module(hidden, positions, mask, past_key_values=plain)
+        assert compressed_kv_info(module)['direct_prefill_calls'] == 0
+        configure_compressed_kv_attention(module, True, prefill=True)
+        actual, weights = module(hidden, positions, mask, past_key_values=direct)
+    assert weights is None
+    torch.testing.assert_close(actual, expected, rtol=.03, atol=.004)
+    info = compressed_kv_info(module)
+    assert info['direct_prefill_calls'] == 1 and info['direct_verify_calls'] == 0
+    assert direct.get_seq_length() == ref.get_seq_length()
+    assert torch.equal(direct.layers[0].keys, ref.layers[0].keys)
+    u = ref.layers[0].key_bank.units
+    assert direct.layers[0].key_bank.units == u
+    assert torch.equal(direct.layers[0].key_bank.data[:, :, :u], ref.layers[0].key_bank.data[:, :, :u])

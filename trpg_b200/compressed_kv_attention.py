@@ -11,7 +11,11 @@ Mirror of ``models/compressed_kv_attention.py`` over the B200 kernels:
   ``configure_compressed_kv_attention`` (``:85-95``) and
   ``compressed_kv_info`` (``:98-103``).  ``_forward`` additionally routes
   2..4-token calls to ``compressed_kv_verify`` inside
-  ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``).
+  ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``), and
+  16..4096-token chunks over a packed history to ``compressed_kv_prefill``
+  (``trpg_b200.compressed_prefill_attention``) when configured with
+  ``prefill=True``; the reference only exposes that kernel as a standalone
+  API.
 
 Kernel launch errors raise; only "unsupported" returns ``None``.
 """
@@ -108,9 +112,10 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
         layer = past_key_values.layers[self.layer_idx]
     q_len = hidden_states.shape[1] if hidden_states.ndim == 3 else 0
     verify = q_len > 1 and q_len <= 4 and mtp_verification_enabled()
+    prefill = 16 <= q_len <= 4096 and getattr(self, '_direct_kv_prefill', False)
     eligible = (self._direct_kv_enabled and not self.training and not torch.is_grad_enabled()
                 and not torch.is_autocast_enabled('cuda') and hidden_states.is_cuda
-                and hidden_states.shape[0] == 1 and (q_len == 1 or verify)
+                and hidden_states.shape[0] == 1 and (q_len == 1 or verify or prefill)
                 and hidden_states.dtype in (torch.bfloat16, torch.float16)
                 and isinstance(layer, QuantizedAttentionLayer) and layer.key_bank.units > 0
                 and self.head_dim in (64, 128, 256) and self.config._attn_implementation == 'sdpa'
@@ -133,8 +138,11 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
     view = layer.append_for_attention(key, value)
     if q_len == 1:
         output = compressed_kv_decode(query, view, self.scaling)
-    else:
+    elif verify:
         output = compressed_kv_verify(query, view, self.scaling)
+    else:
+        from .compressed_prefill_attention import compressed_kv_prefill
+        output = compressed_kv_prefill(query, view, self.scaling)
     if output is None:
         # State was appended once: finish the same operation with SDPA rather
         # than running upstream and appending these tokens a second time.
@@ -148,16 +156,22 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
                                                                   enable_gqa=True, scale=self.scaling)
     else:
         self._direct_kv_calls += 1
-        if q_len > 1:
+        if verify:
             self._direct_kv_verify_calls += 1
+        elif q_len > 1:
+            self._direct_kv_prefill_calls += 1
         self._direct_kv_last_length = view.length
     layer.compact_residual()
     output = output.transpose(1, 2).reshape(*shape, -1).contiguous()
     return self.o_proj(output * torch.sigmoid(gate)), None
 
 
-def configure_compressed_kv_attention(model, enabled=True):
-    """Patch every ``Qwen3_5Attention`` (reference ``:85-95``)."""
+def configure_compressed_kv_attention(model, enabled=True, prefill=False):
+    """Patch every ``Qwen3_5Attention`` (reference ``:85-95``).
+
+    ``prefill=True`` also sends 16..4096-token chunks over a packed history
+    to the packed prefill kernel instead of dequantize + SDPA.
+    """
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     for module in model.modules():
         if type(module) is not Qwen3_5Attention:
@@ -165,9 +179,10 @@ def configure_compressed_kv_attention(model, enabled=True):
         if not hasattr(module, '_direct_kv_original'):
             module._direct_kv_original = module.forward
             module._direct_kv_calls = module._direct_kv_last_length = 0
-            module._direct_kv_verify_calls = 0
+            module._direct_kv_verify_calls = module._direct_kv_prefill_calls = 0
             module.forward = MethodType(_forward, module)
         module._direct_kv_enabled = bool(enabled)
+        module._direct_kv_prefill = bool(prefill)
     return compressed_kv_info(model)
 
 
@@ -177,5 +192,7 @@ def compressed_kv_info(model):
     return dict(backend=BACKEND, configured_layers=sum(m._direct_kv_enabled for m in modules),
                 direct_decode_calls=sum(m._direct_kv_calls for m in modules),
                 direct_verify_calls=sum(getattr(m, '_direct_kv_verify_calls', 0) for m in modules),
+                direct_prefill_calls=sum(getattr(m, '_direct_kv_prefill_calls', 0) for m in modules),
                 longest_decode=max((m._direct_kv_last_length for m in modules), default=0),
-                fallback='SDPA for prefill, arbitrary masks, unsupported shapes or precision')
+                fallback='SDPA for a first chunk (no packed history), chunks of 5..15 or more than '
+                         '4096 tokens, arbitrary masks, unsupported shapes or precision')

@@ -14,13 +14,12 @@
 //     position n iff t <= R - q_len + n, lower-right alignment (:81-90);
 //   * out = accum / denom, stored in the query dtype, [Hq, q_len, D] dense.
 //
-// B200 layout of the work: one CTA per (KV head, tile of 64 query rows),
+// B200 layout of the work: one CTA per (KV head, tile of 128 query rows),
 // where a query row is (position n, group head g) in n-major order, so the
 // G query heads that share a KV head share every dequantized K/V tile (the
 // reference launches one program per query head and dequantizes G times).
-// Four warps, 16 rows each; logits and P.V on mma.sync m16n8k16 with fp32
-// accumulators; K/V tiles of BT tokens (64, or 32 at D = 256 to bound the
-// registers) staged in shared memory:
+// Eight warps, 16 rows each; logits and P.V on mma.sync m16n8k16 with fp32
+// accumulators; K/V tiles of BT = 64 tokens staged in shared memory:
 //   packed K   channel-major [D][BT]  (a bank row is one channel over a block)
 //   residual K token-major   [BT][D]
 //   V          token-major   [BT][D]
@@ -34,13 +33,13 @@
 namespace ckv {
 namespace prefill {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int BM = 16 * kWarps;  // query rows per CTA
 
 template <int D>
 struct Cfg {
-  static constexpr int BT = D == 256 ? 32 : 64;  // tokens per K/V tile (divides 128)
+  static constexpr int BT = 64;  // tokens per K/V tile (divides 128)
   static constexpr int QS = D + 8;    // query tile row stride (elements)
   static constexpr int KCS = BT + 8;  // packed K, channel-major [D][BT]
   static constexpr int KRS = D + 8;   // residual K, token-major [BT][D]
@@ -113,13 +112,18 @@ __device__ __forceinline__ void dequant16(const uint4 &raw, float scale, float l
     w[2] = prmt(bl, bh, 0x5140u);
     w[3] = prmt(bl, bh, 0x7362u);
   }
+  // Paired fp32: code = (2^23 + code) - 2^23 exactly, then one rounding of
+  // fma(code, scale, low) per element, as in the scalar form.
+  const float2 sc = make_float2(scale, scale), lw = make_float2(low, low);
+  const float2 nm = make_float2(-kMagic, -kMagic);
   uint32_t o[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float c0 = byte_magic<0>(w[i]) - kMagic, c1 = byte_magic<1>(w[i]) - kMagic;
-    const float c2 = byte_magic<2>(w[i]) - kMagic, c3 = byte_magic<3>(w[i]) - kMagic;
-    o[2 * i] = E::pack2(__fmaf_rn(c0, scale, low), __fmaf_rn(c1, scale, low));
-    o[2 * i + 1] = E::pack2(__fmaf_rn(c2, scale, low), __fmaf_rn(c3, scale, low));
+    const float2 c01 = __fadd2_rn(make_float2(byte_magic<0>(w[i]), byte_magic<1>(w[i])), nm);
+    const float2 c23 = __fadd2_rn(make_float2(byte_magic<2>(w[i]), byte_magic<3>(w[i])), nm);
+    const float2 x01 = __ffma2_rn(c01, sc, lw), x23 = __ffma2_rn(c23, sc, lw);
+    o[2 * i] = E::pack2(x01.x, x01.y);
+    o[2 * i + 1] = E::pack2(x23.x, x23.y);
   }
   lo = make_uint4(o[0], o[1], o[2], o[3]);
   hi = make_uint4(o[4], o[5], o[6], o[7]);
@@ -284,12 +288,16 @@ __device__ __forceinline__ void tile_math(uint32_t qs, uint32_t ks, uint32_t vs,
     }
   l[0] = l[0] * alpha[0] + rs[0];
   l[1] = l[1] * alpha[1] + rs[1];
+  // Once the row maxima settle (alpha exactly 1 for all of the warp's rows)
+  // the rescale is the identity: skip it.
+  if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
 #pragma unroll
-  for (int nt = 0; nt < D / 8; ++nt) {
-    o[nt][0] *= alpha[0];
-    o[nt][1] *= alpha[0];
-    o[nt][2] *= alpha[1];
-    o[nt][3] *= alpha[1];
+    for (int nt = 0; nt < D / 8; ++nt) {
+      o[nt][0] *= alpha[0];
+      o[nt][1] *= alpha[0];
+      o[nt][2] *= alpha[1];
+      o[nt][3] *= alpha[1];
+    }
   }
 #pragma unroll
   for (int kt = 0; kt < BT / 16; ++kt) {
@@ -310,7 +318,7 @@ __device__ __forceinline__ void tile_math(uint32_t qs, uint32_t ks, uint32_t vs,
 }
 
 template <int BITS, int D, int DT>
-__global__ void __launch_bounds__(kThreads, 2) prefill_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ Params p) {
   using C = Cfg<D>;
   using E = Elem<DT>;
   constexpr int BT = C::BT;
