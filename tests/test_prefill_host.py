@@ -68,3 +68,19 @@ def test_prefill_rejects_bad_arguments_before_any_launch():
         assert lib.ckv_prefill(ctypes.byref(_args(**{k: v})), None) == 1, k
     assert lib.ckv_prefill(ctypes.byref(_args(head_dim=96)), None) == 2
     assert lib.ckv_prefill(ctypes.byref(_args(resid_begin=8)), None) == 2   # a shard
+
+
+def test_install_routes_the_reference_prefill_kernel_module():
+    """``install()`` maps the reference's ``compressed_prefill_kernels`` (whose
+    ``prefill`` its guard imports, models/compressed_prefill_attention.py:46-51)
+    to this package's, and ``uninstall()`` restores the previous entry."""
+    from trpg_b200 import compressed_prefill_kernels, install
+    name = 'refpkg_for_test.compressed_prefill_kernels'
+    assert name not in sys.modules
+    install.install('refpkg_for_test')
+    try:
+        assert sys.modules[name] is compressed_prefill_kernels
+        assert callable(sys.modules[name].prefill)
+    finally:
+        install.uninstall('refpkg_for_test')
+    assert name not in sys.modules

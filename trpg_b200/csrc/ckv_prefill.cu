@@ -189,14 +189,18 @@ __device__ __forceinline__ void write_packed(const PackedRegs<BITS, D> &r, uint3
     sts128(a + 16, hi);
   }
   constexpr int CH = D / 16;
+  // Eight lanes write 32-byte pieces of one token row: lanes 4..7 store
+  // their upper halves first, so each store instruction covers all 32 banks
+  // once (with CH = 4 the two rows' padding already does that).
+  const bool swap = CH >= 8 && (tid & 4);
 #pragma unroll
   for (int j = 0; j < C::V_TASKS; ++j) {
     const int i = tid + j * kThreads, t = i / CH, c0 = (i % CH) * 16;
     uint4 lo, hi;
     dequant16<BITS, DT>(r.v[j], r.vm[j].x, r.vm[j].y, lo, hi);
     const uint32_t a = vs + uint32_t(t * C::VS + c0) * 2;
-    sts128(a, lo);
-    sts128(a + 16, hi);
+    sts128(swap ? a + 16 : a, swap ? hi : lo);
+    sts128(swap ? a : a + 16, swap ? lo : hi);
   }
 }
 
