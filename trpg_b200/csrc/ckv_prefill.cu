@@ -28,6 +28,7 @@
 // after it; residual tiles arrive by cp.async.
 #include "ckv_common.cuh"
 
+#include <atomic>
 #include <cmath>
 
 namespace ckv {
@@ -458,9 +459,15 @@ template <int BITS, int D, int DT>
 int launch(const ckv_prefill_args &a, cudaStream_t st) {
   using C = Cfg<D>;
   auto kern = prefill_kernel<BITS, D, DT>;
-  static const cudaError_t attr =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (attr != cudaSuccess) return cuda_status(attr);
+  // The shared-memory opt-in is a per-device function attribute.
+  static std::atomic<int> configured[64];
+  int dev = 0;
+  CKV_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CKV_ERR_INVALID;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    CKV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured[dev].store(1, std::memory_order_release);
+  }
   const ckv_seq &s = a.seq;
   Params p;
   p.q = s.query;
