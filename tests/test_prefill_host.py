@@ -84,3 +84,22 @@ def test_install_routes_the_reference_prefill_kernel_module():
     finally:
         install.uninstall('refpkg_for_test')
     assert name not in sys.modules
+
+
+def test_patch_prefill_limits():
+    """Prefill routing limits of the attention patch: 1024 tokens by default,
+    4096 with ``prefill=True``, none with ``prefill=False``."""
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
+    from trpg_b200.compressed_kv_attention import compressed_kv_info, configure_compressed_kv_attention
+    config = Qwen3_5TextConfig(hidden_size=128, intermediate_size=256, num_hidden_layers=1,
+                               num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                               layer_types=['full_attention'])
+    config._attn_implementation = 'sdpa'
+    module = Qwen3_5Attention(config, 0)
+    limits = []
+    for prefill in (None, True, False):
+        configure_compressed_kv_attention(module, prefill=prefill)
+        limits.append(module._direct_kv_prefill_max)
+    assert limits == [1024, 4096, 0]
+    assert compressed_kv_info(module)['direct_prefill_calls'] == 0

@@ -12,10 +12,11 @@ Mirror of ``models/compressed_kv_attention.py`` over the B200 kernels:
   ``compressed_kv_info`` (``:98-103``).  ``_forward`` additionally routes
   2..4-token calls to ``compressed_kv_verify`` inside
   ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``), and
-  16..4096-token chunks over a packed history to ``compressed_kv_prefill``
-  (``trpg_b200.compressed_prefill_attention``) when configured with
-  ``prefill=True``; the reference only exposes that kernel as a standalone
-  API.
+  chunks over a packed history to ``compressed_kv_prefill``
+  (``trpg_b200.compressed_prefill_attention``): 16..1024 tokens by default,
+  where the packed kernel is faster than dequantize + SDPA, and up to 4096
+  with ``prefill=True``.  The reference only exposes that kernel as a
+  standalone API.
 
 Kernel launch errors raise; only "unsupported" returns ``None``.
 """
@@ -112,7 +113,7 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
         layer = past_key_values.layers[self.layer_idx]
     q_len = hidden_states.shape[1] if hidden_states.ndim == 3 else 0
     verify = q_len > 1 and q_len <= 4 and mtp_verification_enabled()
-    prefill = 16 <= q_len <= 4096 and getattr(self, '_direct_kv_prefill', False)
+    prefill = 16 <= q_len <= getattr(self, '_direct_kv_prefill_max', 0)
     eligible = (self._direct_kv_enabled and not self.training and not torch.is_grad_enabled()
                 and not torch.is_autocast_enabled('cuda') and hidden_states.is_cuda
                 and hidden_states.shape[0] == 1 and (q_len == 1 or verify or prefill)
@@ -166,11 +167,13 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
     return self.o_proj(output * torch.sigmoid(gate)), None
 
 
-def configure_compressed_kv_attention(model, enabled=True, prefill=False):
+def configure_compressed_kv_attention(model, enabled=True, prefill=None):
     """Patch every ``Qwen3_5Attention`` (reference ``:85-95``).
 
-    ``prefill=True`` also sends 16..4096-token chunks over a packed history
-    to the packed prefill kernel instead of dequantize + SDPA.
+    Prefill chunks over a packed history go to the packed prefill kernel
+    instead of dequantize + SDPA: chunks of 16..1024 tokens by default
+    (``prefill=None``), 16..4096 with ``prefill=True``, none with
+    ``prefill=False``.
     """
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     for module in model.modules():
@@ -182,7 +185,7 @@ def configure_compressed_kv_attention(model, enabled=True, prefill=False):
             module._direct_kv_verify_calls = module._direct_kv_prefill_calls = 0
             module.forward = MethodType(_forward, module)
         module._direct_kv_enabled = bool(enabled)
-        module._direct_kv_prefill = bool(prefill)
+        module._direct_kv_prefill_max = 1024 if prefill is None else (4096 if prefill else 0)
     return compressed_kv_info(model)
 
 
@@ -194,5 +197,5 @@ def compressed_kv_info(model):
                 direct_verify_calls=sum(getattr(m, '_direct_kv_verify_calls', 0) for m in modules),
                 direct_prefill_calls=sum(getattr(m, '_direct_kv_prefill_calls', 0) for m in modules),
                 longest_decode=max((m._direct_kv_last_length for m in modules), default=0),
-                fallback='SDPA for a first chunk (no packed history), chunks of 5..15 or more than '
-                         '4096 tokens, arbitrary masks, unsupported shapes or precision')
+                fallback='SDPA for a first chunk (no packed history), chunks of 5..15 tokens or '
+                         'above the prefill limit, arbitrary masks, unsupported shapes or precision')
