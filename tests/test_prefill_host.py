@@ -87,8 +87,8 @@ def test_install_routes_the_reference_prefill_kernel_module():
 
 
 def test_patch_prefill_limits():
-    """Prefill routing limits of the attention patch: 1024 tokens by default,
-    4096 with ``prefill=True``, none with ``prefill=False``."""
+    """Prefill routing limits of the attention patch: none by default, 4096
+    tokens with ``prefill=True``."""
     from transformers import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     from trpg_b200.compressed_kv_attention import compressed_kv_info, configure_compressed_kv_attention
@@ -98,8 +98,10 @@ def test_patch_prefill_limits():
     config._attn_implementation = 'sdpa'
     module = Qwen3_5Attention(config, 0)
     limits = []
-    for prefill in (None, True, False):
+    configure_compressed_kv_attention(module)
+    limits.append(module._direct_kv_prefill_max)
+    for prefill in (True, False):
         configure_compressed_kv_attention(module, prefill=prefill)
         limits.append(module._direct_kv_prefill_max)
-    assert limits == [1024, 4096, 0]
+    assert limits == [0, 4096, 0]
     assert compressed_kv_info(module)['direct_prefill_calls'] == 0
