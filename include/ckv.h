@@ -253,7 +253,11 @@ int ckv_combine_partials(const float *partials, int parts, int64_t rows, int hea
  *        unit_begin = 0, unit_end = P/128, resid_begin = 0, resid_end = R.
  * Needs P >= 128 and R >= qlen.  Residual token t is visible to query
  * position n iff t <= R - qlen + n; every packed token is visible.
- * Scratch-free: one launch, no workspace.
+ *
+ * One CTA per (KV head, 128 query rows).  When that grid is short of one
+ * CTA per SM (chunks of about 512 tokens or fewer), the packed history is
+ * split across more CTAs; they write (o, m, l) partial records to the
+ * workspace and a ckv_combine_partials launch writes `out`.
  */
 typedef struct {
   ckv_seq seq;
@@ -261,7 +265,14 @@ typedef struct {
   float scale;                  /* softmax scale applied to q.k */
 } ckv_prefill_args;
 
-int ckv_prefill(const ckv_prefill_args *args, ckv_stream_t stream);
+/* Workspace bytes ckv_prefill needs for `args` (0 when the history is not
+ * split; host only: reads the current device's SM count, launches nothing). */
+int ckv_prefill_workspace(const ckv_prefill_args *args, size_t *bytes);
+
+/* workspace: ckv_prefill_workspace() bytes, 16-byte aligned (may be NULL
+ * when that is 0). */
+int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t workspace_bytes,
+                ckv_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -23,8 +23,11 @@ class PrefillArgs(ctypes.Structure):
 
 def _lib():
     lib = _native.library()
-    lib.ckv_prefill.argtypes = [ctypes.POINTER(PrefillArgs), ctypes.c_void_p]
+    lib.ckv_prefill.argtypes = [ctypes.POINTER(PrefillArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                ctypes.c_void_p]
     lib.ckv_prefill.restype = ctypes.c_int
+    lib.ckv_prefill_workspace.argtypes = [ctypes.POINTER(PrefillArgs), ctypes.POINTER(ctypes.c_size_t)]
+    lib.ckv_prefill_workspace.restype = ctypes.c_int
     return lib
 
 
@@ -54,7 +57,7 @@ def test_cpu_query_never_imports_or_launches_the_kernel():
 
 def test_prefill_rejects_bad_arguments_before_any_launch():
     lib = _lib()
-    assert lib.ckv_prefill(None, None) == 1
+    assert lib.ckv_prefill(None, None, 0, None) == 1
     bad = {
         'qlen': R + 1,                 # the window must hold the chunk
         'packed_tokens': 0,            # needs packed history
@@ -65,9 +68,30 @@ def test_prefill_rejects_bad_arguments_before_any_launch():
         'keys': 0x10000008,            # residual base not 16-byte aligned
     }
     for k, v in bad.items():
-        assert lib.ckv_prefill(ctypes.byref(_args(**{k: v})), None) == 1, k
-    assert lib.ckv_prefill(ctypes.byref(_args(head_dim=96)), None) == 2
-    assert lib.ckv_prefill(ctypes.byref(_args(resid_begin=8)), None) == 2   # a shard
+        assert lib.ckv_prefill(ctypes.byref(_args(**{k: v})), None, 0, None) == 1, k
+    assert lib.ckv_prefill(ctypes.byref(_args(head_dim=96)), None, 0, None) == 2
+    assert lib.ckv_prefill(ctypes.byref(_args(resid_begin=8)), None, 0, None) == 2   # a shard
+
+
+def test_short_chunks_split_the_history_and_need_a_workspace():
+    """32 queries x 2 group heads = 1 tile per KV head, 2 CTAs: the history
+    (256 packed tokens = 4 tiles of 64) splits 4 ways, one (o, m, l) record of
+    D + 2 floats per split and output row.  Without a GPU the plan assumes
+    148 SMs.  A missing workspace is refused before any launch."""
+    lib = _lib()
+    nbytes = ctypes.c_size_t()
+    assert lib.ckv_prefill_workspace(ctypes.byref(_args()), ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 4 * (4 * QLEN) * (D + 2) * 4
+    assert lib.ckv_prefill(ctypes.byref(_args()), None, 0, None) == 3
+    # 1184 queries x 2 = 19 tiles per KV head, 38 CTAs: 3 splits by SM count,
+    # but a 128-token history has only 2 tiles of 64, so 2.
+    big = _args(qlen=1184, packed_tokens=128, length=128 + 1200, unit_end=1, resid_end=1200)
+    assert lib.ckv_prefill_workspace(ctypes.byref(big), ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 2 * (4 * 1184) * (D + 2) * 4
+    # 4096 queries x 2 = 64 tiles x 2 heads = 128 CTAs: below 148 but 148 // 128 = 1.
+    full = _args(qlen=4096, length=P + 4096, resid_end=4096)
+    assert lib.ckv_prefill_workspace(ctypes.byref(full), ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 0
 
 
 def test_install_routes_the_reference_prefill_kernel_module():

@@ -20,7 +20,7 @@ TORCH_LIB_PATH = PKG / '_ckv_torch.so'
 EXPORTS = ('ckv_status_string', 'ckv_last_error', 'ckv_version', 'ckv_pack_rows',
            'ckv_unpack_rows', 'ckv_pack_append', 'ckv_residual_append', 'ckv_attention_workspace',
            'ckv_attention_error', 'ckv_attention', 'ckv_attention_static',
-           'ckv_combine_partials', 'ckv_prefill')
+           'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill')
 
 ROUNDING = {'half_even': 0, 'half_up': 1}
 

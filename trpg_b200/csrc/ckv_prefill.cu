@@ -28,10 +28,14 @@
 // after it; residual tiles arrive by cp.async.
 #include "ckv_common.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 
 namespace ckv {
+namespace attn {
+int sm_count();  // SMs of the current device (148 without one), ckv_attn.cu
+}
 namespace prefill {
 
 constexpr int kWarps = 8;
@@ -76,6 +80,8 @@ struct Params {
   void *out;
   int qlen, packed, resid, groups;
   float scale_log2;
+  int splits;        // history splits (grid z); > 1 writes partial records
+  float *partials;   // [splits][Hq * qlen][D + 2] fp32 when splits > 1
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
@@ -363,19 +369,24 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int gr = r0 + warp * 16 + (lane >> 2) + 8 * h;
     vis[h] = p.resid - p.qlen + gr / G;
   }
+  // History split z of p.splits: packed tiles [i0, i1); the last split also
+  // takes the residual window.
+  const int z = blockIdx.z, ntiles = p.packed / BT;
+  const int i0 = int(int64_t(ntiles) * z / p.splits), i1 = int(int64_t(ntiles) * (z + 1) / p.splits);
+  const int np = i1 - i0;
   const int last_row = min(r0 + BM, nrows) - 1;
   const int rstop = min(p.resid, p.resid - p.qlen + last_row / G + 1);
-  const int np = p.packed / BT, nr = (rstop + BT - 1) / BT;
+  const int nr = z == p.splits - 1 ? (rstop + BT - 1) / BT : 0;
 
   // Packed history, double-buffered through registers.
   {
     PackedRegs<BITS, D> pr;
-    read_packed<BITS, D>(p, kvh, 0, tid, pr);
+    read_packed<BITS, D>(p, kvh, i0 * BT, tid, pr);
     write_packed<BITS, D, DT>(pr, kbuf[0], vbuf[0], tid);
     __syncthreads();
     for (int i = 0; i < np; ++i) {
       const int b = i & 1;
-      if (i + 1 < np) read_packed<BITS, D>(p, kvh, (i + 1) * BT, tid, pr);
+      if (i + 1 < np) read_packed<BITS, D>(p, kvh, (i0 + i + 1) * BT, tid, pr);
       tile_math<D, DT, true>(qs, kbuf[b], vbuf[b], warp, lane, o, m, l, p.scale_log2, 0, 0, vis);
       if (i + 1 < np) write_packed<BITS, D, DT>(pr, kbuf[b ^ 1], vbuf[b ^ 1], tid);
       __syncthreads();
@@ -398,12 +409,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     __syncthreads();
   }
 
-  // out = accum / denom in the query dtype; rows past the chunk are dropped.
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
     l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
   }
+  if (p.splits > 1) {
+    // Partial record of output row (head, pos) for split z, the layout
+    // ckv_combine_partials merges: sum 2^(s - m) v over this split's tokens,
+    // then m (log2 domain) and l = sum 2^(s - m).
+    const int64_t orows = int64_t(p.qlen) * G * gridDim.y;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int gr = r0 + warp * 16 + (lane >> 2) + 8 * h;
+      if (gr >= nrows) continue;
+      const int pos = gr / G, head = kvh * G + gr % G;
+      float *rec = p.partials + (int64_t(z) * orows + int64_t(head) * p.qlen + pos) * (D + 2);
+#pragma unroll
+      for (int nt = 0; nt < D / 8; ++nt)
+        *reinterpret_cast<float2 *>(rec + nt * 8 + 2 * (lane & 3)) =
+            make_float2(o[nt][2 * h], o[nt][2 * h + 1]);
+      if ((lane & 3) == 0) *reinterpret_cast<float2 *>(rec + D) = make_float2(m[h], l[h]);
+    }
+    return;
+  }
+  // out = accum / denom in the query dtype; rows past the chunk are dropped.
   uint16_t *out = static_cast<uint16_t *>(p.out);
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -455,8 +485,29 @@ int validate(const ckv_prefill_args &a) {
   return CKV_OK;
 }
 
+// History splits: a grid of (query tiles x KV heads) short of one CTA per SM
+// splits the packed history so that the grid fills the SMs (at most one
+// split per packed tile); the splits' partial records are then merged.
+struct Plan {
+  int tiles = 0, splits = 1;
+  size_t bytes = 0;  // workspace for the partial records
+};
+
+Plan make_plan(const ckv_prefill_args &a) {
+  Plan pl;
+  const int64_t rows = int64_t(a.qlen) * (a.heads_q / a.heads_kv);
+  pl.tiles = int((rows + BM - 1) / BM);
+  const int64_t ctas = int64_t(pl.tiles) * a.heads_kv;
+  const int sms = attn::sm_count();
+  const int64_t ntiles = a.seq.packed_tokens / 64;
+  if (ctas < sms) pl.splits = int(std::max<int64_t>(1, std::min<int64_t>(ntiles, sms / ctas)));
+  if (pl.splits > 1)
+    pl.bytes = size_t(pl.splits) * size_t(a.heads_q) * size_t(a.qlen) * size_t(a.head_dim + 2) * 4;
+  return pl;
+}
+
 template <int BITS, int D, int DT>
-int launch(const ckv_prefill_args &a, cudaStream_t st) {
+int launch(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
   using C = Cfg<D>;
   auto kern = prefill_kernel<BITS, D, DT>;
   // The shared-memory opt-in is a per-device function attribute.
@@ -497,34 +548,53 @@ int launch(const ckv_prefill_args &a, cudaStream_t st) {
   p.resid = int(s.length - s.packed_tokens);
   p.groups = a.heads_q / a.heads_kv;
   p.scale_log2 = float(double(a.scale) * 1.4426950408889634);
-  const int64_t rows = int64_t(a.qlen) * p.groups;
-  const dim3 grid(unsigned((rows + BM - 1) / BM), unsigned(a.heads_kv));
+  p.splits = pl.splits;
+  p.partials = static_cast<float *>(workspace);
+  const dim3 grid(unsigned(pl.tiles), unsigned(a.heads_kv), unsigned(pl.splits));
   kern<<<grid, kThreads, C::SMEM, st>>>(p);
-  return cuda_status(cudaGetLastError());
+  CKV_CUDA_TRY(cudaGetLastError());
+  if (pl.splits == 1) return CKV_OK;
+  return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, s.out,
+                              reinterpret_cast<ckv_stream_t>(st));
 }
 
 template <int BITS, int D>
-int dispatch_dt(const ckv_prefill_args &a, cudaStream_t st) {
-  return a.dtype == CKV_BF16 ? launch<BITS, D, CKV_BF16>(a, st) : launch<BITS, D, CKV_F16>(a, st);
+int dispatch_dt(const ckv_prefill_args &a, const Plan &pl, void *ws, cudaStream_t st) {
+  return a.dtype == CKV_BF16 ? launch<BITS, D, CKV_BF16>(a, pl, ws, st)
+                             : launch<BITS, D, CKV_F16>(a, pl, ws, st);
 }
 
 template <int BITS>
-int dispatch_d(const ckv_prefill_args &a, cudaStream_t st) {
+int dispatch_d(const ckv_prefill_args &a, const Plan &pl, void *ws, cudaStream_t st) {
   switch (a.head_dim) {
-    case 64: return dispatch_dt<BITS, 64>(a, st);
-    case 128: return dispatch_dt<BITS, 128>(a, st);
-    default: return dispatch_dt<BITS, 256>(a, st);
+    case 64: return dispatch_dt<BITS, 64>(a, pl, ws, st);
+    case 128: return dispatch_dt<BITS, 128>(a, pl, ws, st);
+    default: return dispatch_dt<BITS, 256>(a, pl, ws, st);
   }
 }
 
 }  // namespace prefill
 }  // namespace ckv
 
-extern "C" int ckv_prefill(const ckv_prefill_args *args, ckv_stream_t stream) {
+extern "C" int ckv_prefill_workspace(const ckv_prefill_args *args, size_t *bytes) {
+  using namespace ckv::prefill;
+  if (!args || !bytes) return CKV_ERR_INVALID;
+  const int v = validate(*args);
+  if (v != CKV_OK) return v;
+  *bytes = make_plan(*args).bytes;
+  return CKV_OK;
+}
+
+extern "C" int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t workspace_bytes,
+                           ckv_stream_t stream) {
   using namespace ckv::prefill;
   if (!args) return CKV_ERR_INVALID;
   const int v = validate(*args);
   if (v != CKV_OK) return v;
+  const Plan pl = make_plan(*args);
+  if (pl.bytes && (!workspace || workspace_bytes < pl.bytes || !al(workspace, 16)))
+    return CKV_ERR_WORKSPACE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  return args->bits == 8 ? dispatch_d<8>(*args, st) : dispatch_d<4>(*args, st);
+  return args->bits == 8 ? dispatch_d<8>(*args, pl, workspace, st)
+                         : dispatch_d<4>(*args, pl, workspace, st);
 }

@@ -482,7 +482,12 @@ Tensor prefill(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor
   a.bits = int32_t(bits);
   a.dtype = dtype_code(q.scalar_type());
   a.scale = float(scale);
-  check_status(ckv_prefill(&a, current_stream(q)), "prefill");
+  size_t bytes = 0;
+  check_status(ckv_prefill_workspace(&a, &bytes), "prefill_workspace");
+  Tensor ws;
+  if (bytes)
+    ws = at::empty({int64_t((bytes + 3) / 4)}, q.options().dtype(at::kFloat));
+  check_status(ckv_prefill(&a, bytes ? ws.data_ptr() : nullptr, bytes, current_stream(q)), "prefill");
   return out;
 }
 
