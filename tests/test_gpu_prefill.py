@@ -160,7 +160,7 @@ def test_real_qwen_attention_routes_a_prefill_chunk_and_keeps_the_cache():
         configure_compressed_kv_attention(module, True, prefill=False)   # prefill routing off
         module(hidden, positions, mask, past_key_values=plain)
         assert compressed_kv_info(module)['direct_prefill_calls'] == 0
-        configure_compressed_kv_attention(module, True, prefill=True)
+        configure_compressed_kv_attention(module, True)          # default: chunks up to 1024
         actual, weights = module(hidden, positions, mask, past_key_values=direct)
     assert weights is None
     torch.testing.assert_close(actual, expected, rtol=.03, atol=.004)

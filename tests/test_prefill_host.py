@@ -111,8 +111,8 @@ def test_install_routes_the_reference_prefill_kernel_module():
 
 
 def test_patch_prefill_limits():
-    """Prefill routing limits of the attention patch: none by default, 4096
-    tokens with ``prefill=True``."""
+    """Prefill routing limits of the attention patch: 1024 tokens by default,
+    4096 with ``prefill=True``, none with ``prefill=False``."""
     from transformers import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     from trpg_b200.compressed_kv_attention import compressed_kv_info, configure_compressed_kv_attention
@@ -127,5 +127,5 @@ def test_patch_prefill_limits():
     for prefill in (True, False):
         configure_compressed_kv_attention(module, prefill=prefill)
         limits.append(module._direct_kv_prefill_max)
-    assert limits == [0, 4096, 0]
+    assert limits == [1024, 4096, 0]
     assert compressed_kv_info(module)['direct_prefill_calls'] == 0
