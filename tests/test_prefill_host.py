@@ -88,10 +88,16 @@ def test_short_chunks_split_the_history_and_need_a_workspace():
     big = _args(qlen=1184, packed_tokens=128, length=128 + 1200, unit_end=1, resid_end=1200)
     assert lib.ckv_prefill_workspace(ctypes.byref(big), ctypes.byref(nbytes)) == 0
     assert nbytes.value == 2 * (4 * 1184) * (D + 2) * 4
-    # 4096 queries x 2 = 64 tiles x 2 heads = 128 CTAs: below 148 but 148 // 128 = 1.
+    # 4096 queries x 2 = 64 tiles x 2 heads = 128 CTAs fill 86% of a wave, and
+    # 2..4 splits fill 256/296, 384/444, 512/592 just the same: no split.
     full = _args(qlen=4096, length=P + 4096, resid_end=4096)
     assert lib.ckv_prefill_workspace(ctypes.byref(full), ctypes.byref(nbytes)) == 0
     assert nbytes.value == 0
+    # 4 KV heads: 256 CTAs are 1.73 waves; 4 splits make 1024 CTAs, 7 waves
+    # less 12 slots (99% full).
+    wide = _args(qlen=4096, length=P + 4096, resid_end=4096, heads_q=8, heads_kv=4)
+    assert lib.ckv_prefill_workspace(ctypes.byref(wide), ctypes.byref(nbytes)) == 0
+    assert nbytes.value == 4 * (8 * 4096) * (D + 2) * 4
 
 
 def test_install_routes_the_reference_prefill_kernel_module():

@@ -371,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   }
   // History split z of p.splits: packed tiles [i0, i1); the last split also
   // takes the residual window.
-  const int z = blockIdx.z, ntiles = p.packed / BT;
+  // The split with the residual window (the most work) launches first.
+  const int z = p.splits - 1 - int(blockIdx.z), ntiles = p.packed / BT;
   const int i0 = int(int64_t(ntiles) * z / p.splits), i1 = int(int64_t(ntiles) * (z + 1) / p.splits);
   const int np = i1 - i0;
   const int last_row = min(r0 + BM, nrows) - 1;
@@ -485,9 +486,11 @@ int validate(const ckv_prefill_args &a) {
   return CKV_OK;
 }
 
-// History splits: a grid of (query tiles x KV heads) short of one CTA per SM
-// splits the packed history so that the grid fills the SMs (at most one
-// split per packed tile); the splits' partial records are then merged.
+// History splits: the packed history is split so that the grid of (query
+// tiles x KV heads x splits) fills whole waves of one CTA per SM -- a short
+// grid up to one wave, a longer one (at most 4 splits) to fewer idle SMs in
+// its last wave.  The fewest splits within 2% of the best fill win, at most
+// one split per 64-token tile; the splits' partial records are then merged.
 struct Plan {
   int tiles = 0, splits = 1;
   size_t bytes = 0;  // workspace for the partial records
@@ -500,7 +503,16 @@ Plan make_plan(const ckv_prefill_args &a) {
   const int64_t ctas = int64_t(pl.tiles) * a.heads_kv;
   const int sms = attn::sm_count();
   const int64_t ntiles = a.seq.packed_tokens / 64;
-  if (ctas < sms) pl.splits = int(std::max<int64_t>(1, std::min<int64_t>(ntiles, sms / ctas)));
+  const int64_t smax = std::min<int64_t>(ntiles, std::max<int64_t>(4, sms / std::max<int64_t>(ctas, 1)));
+  double best = 0.0;
+  for (int64_t sp = 1; sp <= smax; ++sp) {
+    const int64_t n = ctas * sp, waves = (n + sms - 1) / sms;
+    const double fill = double(n) / double(waves * sms);
+    if (fill > best + 0.02) {
+      best = fill;
+      pl.splits = int(sp);
+    }
+  }
   if (pl.splits > 1)
     pl.bytes = size_t(pl.splits) * size_t(a.heads_q) * size_t(a.qlen) * size_t(a.head_dim + 2) * 4;
   return pl;
