@@ -369,18 +369,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int gr = r0 + warp * 16 + (lane >> 2) + 8 * h;
     vis[h] = p.resid - p.qlen + gr / G;
   }
-  // History split z of p.splits: packed tiles [i0, i1); the last split also
-  // takes the residual window.
-  // The split with the residual window (the most work) launches first.
+  // History split z of p.splits: an even share of this CTA's items, its
+  // packed tiles followed by its residual tiles (up to its last visible
+  // token).  The split with the most recent tokens launches first.
   const int z = p.splits - 1 - int(blockIdx.z), ntiles = p.packed / BT;
-  const int i0 = int(int64_t(ntiles) * z / p.splits), i1 = int(int64_t(ntiles) * (z + 1) / p.splits);
-  const int np = i1 - i0;
   const int last_row = min(r0 + BM, nrows) - 1;
   const int rstop = min(p.resid, p.resid - p.qlen + last_row / G + 1);
-  const int nr = z == p.splits - 1 ? (rstop + BT - 1) / BT : 0;
+  const int total = ntiles + (rstop + BT - 1) / BT;
+  const int a0 = int(int64_t(total) * z / p.splits), a1 = int(int64_t(total) * (z + 1) / p.splits);
+  const int i0 = min(a0, ntiles), np = min(a1, ntiles) - i0;
+  const int rb = max(a0, ntiles) - ntiles, nr = max(a1, ntiles) - ntiles - rb;
 
   // Packed history, double-buffered through registers.
-  {
+  if (np > 0) {
     PackedRegs<BITS, D> pr;
     read_packed<BITS, D>(p, kvh, i0 * BT, tid, pr);
     write_packed<BITS, D, DT>(pr, kbuf[0], vbuf[0], tid);
@@ -393,19 +394,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       __syncthreads();
     }
   }
-  // Exact residual window up to this tile's last visible token; tile i sits
-  // in buffer (np + i) & 1, the next one lands while this one is used.
-  if (nr > 0) issue_resid<D>(p, kvh, 0, tid, kbuf[np & 1], vbuf[np & 1]);
+  // Exact residual window, tiles [rb, rb + nr); tile i sits in buffer
+  // (np + i) & 1, the next one lands while this one is used.
+  if (nr > 0) issue_resid<D>(p, kvh, rb * BT, tid, kbuf[np & 1], vbuf[np & 1]);
   for (int i = 0; i < nr; ++i) {
     const int b = (np + i) & 1;
     if (i + 1 < nr) {
-      issue_resid<D>(p, kvh, (i + 1) * BT, tid, kbuf[b ^ 1], vbuf[b ^ 1]);
+      issue_resid<D>(p, kvh, (rb + i + 1) * BT, tid, kbuf[b ^ 1], vbuf[b ^ 1]);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    tile_math<D, DT, false>(qs, kbuf[b], vbuf[b], warp, lane, o, m, l, p.scale_log2, i * BT,
+    tile_math<D, DT, false>(qs, kbuf[b], vbuf[b], warp, lane, o, m, l, p.scale_log2, (rb + i) * BT,
                             p.resid, vis);
     __syncthreads();
   }
@@ -430,7 +431,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
       for (int nt = 0; nt < D / 8; ++nt)
         *reinterpret_cast<float2 *>(rec + nt * 8 + 2 * (lane & 3)) =
             make_float2(o[nt][2 * h], o[nt][2 * h + 1]);
-      if ((lane & 3) == 0) *reinterpret_cast<float2 *>(rec + D) = make_float2(m[h], l[h]);
+      // A row that saw no token in this split (a split of residual tiles all
+      // past its position) records m = -inf: weight 0 in the merge.
+      if ((lane & 3) == 0)
+        *reinterpret_cast<float2 *>(rec + D) = make_float2(l[h] > 0.f ? m[h] : -INFINITY, l[h]);
     }
     return;
   }
@@ -486,11 +490,12 @@ int validate(const ckv_prefill_args &a) {
   return CKV_OK;
 }
 
-// History splits: the packed history is split so that the grid of (query
-// tiles x KV heads x splits) fills whole waves of one CTA per SM -- a short
-// grid up to one wave, a longer one (at most 4 splits) to fewer idle SMs in
-// its last wave.  The fewest splits within 2% of the best fill win, at most
-// one split per 64-token tile; the splits' partial records are then merged.
+// History splits: each CTA's items (packed tiles, then its residual tiles)
+// are split so that the grid of (query tiles x KV heads x splits) fills
+// whole waves of one CTA per SM -- a short grid up to one wave, a longer one
+// (at most 4 splits) to fewer idle SMs in its last wave.  The fewest splits
+// within 2% of the best fill win, at most one split per 64-token packed
+// tile; the splits' partial records are then merged.
 struct Plan {
   int tiles = 0, splits = 1;
   size_t bytes = 0;  // workspace for the partial records
