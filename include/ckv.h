@@ -254,8 +254,8 @@ int ckv_combine_partials(const float *partials, int parts, int64_t rows, int hea
  * Needs P >= 128 and R >= qlen.  Residual token t is visible to query
  * position n iff t <= R - qlen + n; every packed token is visible.
  *
- * One CTA per (KV head, 128 query rows).  When that grid is short of one
- * CTA per SM (chunks of about 512 tokens or fewer), the packed history is
+ * One CTA per (KV head, 128 query rows).  When that grid would leave SMs
+ * idle (short of one wave, or a part-empty last wave), each CTA's history is
  * split across more CTAs; they write (o, m, l) partial records to the
  * workspace and a ckv_combine_partials launch writes `out`.
  */
