@@ -171,3 +171,15 @@ def test_real_qwen_attention_routes_a_prefill_chunk_and_keeps_the_cache():
     u = ref.layers[0].key_bank.units
     assert direct.layers[0].key_bank.units == u
     assert torch.equal(direct.layers[0].key_bank.data[:, :, :u], ref.layers[0].key_bank.data[:, :, :u])
+
+
+@pytest.mark.parametrize('bits,dtype', [(8, 'bfloat16'), (4, 'float16')])
+def test_short_history_long_chunk_splits_into_residual_only_shares(bits, dtype):
+    """128 packed tokens under a 600-token chunk (one query head per KV head):
+    10 CTAs split the history 2 ways, and the second share holds only
+    residual tiles, so its early query rows see no token there (m = -inf in
+    their partial records)."""
+    layer, view, ol = gpu_cache_state(601 + bits, 2, 900, 64, bits, 600, dtype)
+    assert view.packed_tokens == 128
+    qn, qt = query(602, 2, 600, 64, dtype)
+    check(prefill(qt, view, .125), O.decode_reference(qn, ol, .125, causal_lower_right=True))
