@@ -655,15 +655,20 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
 template <int DT>
 __global__ void combine_kernel(const float *__restrict__ parts, int nparts, int64_t rows, int D,
                                typename Elem<DT>::T *__restrict__ out) {
-  const int64_t row = blockIdx.x;
+  // One warp per row, lanes over the channels (coalesced), several rows per
+  // block: a call merges up to Hq x qlen rows.
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
   const size_t stride = size_t(rows) * (D + 2);
+  const float *base = parts + row * (D + 2);
   float M = -INFINITY;
-  for (int k = 0; k < nparts; ++k) M = fmaxf(M, parts[k * stride + row * (D + 2) + D]);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int k = 0; k < nparts; ++k) M = fmaxf(M, base[k * stride + D]);
+  for (int d = lane; d < D; d += 32) {
     float O = 0.f, L = 0.f;
     if (M != -INFINITY) {
       for (int k = 0; k < nparts; ++k) {
-        const float *pr = parts + k * stride + row * (D + 2);
+        const float *pr = base + k * stride;
         const float wt = pr[D] == -INFINITY ? 0.f : ex2(pr[D] - M);
         O += wt * pr[d];
         L += wt * pr[D + 1];
@@ -1039,12 +1044,13 @@ extern "C" int ckv_combine_partials(const float *partials, int parts, int64_t ro
   if (dtype != CKV_BF16 && dtype != CKV_F16) return CKV_ERR_INVALID;
   if (rows == 0) return CKV_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int threads = std::min(256, head_dim);
+  constexpr int kRowsPerBlock = 8;  // one warp each
+  const unsigned blocks = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
   if (dtype == CKV_BF16)
-    combine_kernel<CKV_BF16><<<unsigned(rows), threads, 0, st>>>(
+    combine_kernel<CKV_BF16><<<blocks, 32 * kRowsPerBlock, 0, st>>>(
         partials, parts, rows, head_dim, static_cast<__nv_bfloat16 *>(out));
   else
-    combine_kernel<CKV_F16><<<unsigned(rows), threads, 0, st>>>(partials, parts, rows, head_dim,
-                                                                static_cast<__half *>(out));
+    combine_kernel<CKV_F16><<<blocks, 32 * kRowsPerBlock, 0, st>>>(
+        partials, parts, rows, head_dim, static_cast<__half *>(out));
   return cuda_status(cudaGetLastError());
 }
