@@ -654,17 +654,17 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
 
 template <int DT>
 __global__ void combine_kernel(const float *__restrict__ parts, int nparts, int64_t rows, int D,
-                               typename Elem<DT>::T *__restrict__ out) {
-  // One warp per row, lanes over the channels (coalesced), several rows per
-  // block: a call merges up to Hq x qlen rows.
-  const int64_t row = int64_t(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+                               int tpr, typename Elem<DT>::T *__restrict__ out) {
+  // `tpr` threads per row (32 or the whole block), lanes over the channels
+  // (coalesced): many rows take a warp each, few rows a block each.
+  const int64_t row = int64_t(blockIdx.x) * (blockDim.x / tpr) + threadIdx.x / tpr;
   if (row >= rows) return;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x % tpr;
   const size_t stride = size_t(rows) * (D + 2);
   const float *base = parts + row * (D + 2);
   float M = -INFINITY;
   for (int k = 0; k < nparts; ++k) M = fmaxf(M, base[k * stride + D]);
-  for (int d = lane; d < D; d += 32) {
+  for (int d = lane; d < D; d += tpr) {
     float O = 0.f, L = 0.f;
     if (M != -INFINITY) {
       for (int k = 0; k < nparts; ++k) {
@@ -1044,13 +1044,16 @@ extern "C" int ckv_combine_partials(const float *partials, int parts, int64_t ro
   if (dtype != CKV_BF16 && dtype != CKV_F16) return CKV_ERR_INVALID;
   if (rows == 0) return CKV_OK;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  constexpr int kRowsPerBlock = 8;  // one warp each
-  const unsigned blocks = unsigned((rows + kRowsPerBlock - 1) / kRowsPerBlock);
+  // Enough rows for 16 blocks of 8 warp-rows per SM: a warp per row;
+  // otherwise a 256-thread block per row.
+  const int tpr = rows >= int64_t(sm_count()) * 128 ? 32 : 256;
+  const int64_t per_block = 256 / tpr;
+  const unsigned blocks = unsigned((rows + per_block - 1) / per_block);
   if (dtype == CKV_BF16)
-    combine_kernel<CKV_BF16><<<blocks, 32 * kRowsPerBlock, 0, st>>>(
-        partials, parts, rows, head_dim, static_cast<__nv_bfloat16 *>(out));
+    combine_kernel<CKV_BF16><<<blocks, 256, 0, st>>>(partials, parts, rows, head_dim, tpr,
+                                                     static_cast<__nv_bfloat16 *>(out));
   else
-    combine_kernel<CKV_F16><<<blocks, 32 * kRowsPerBlock, 0, st>>>(
-        partials, parts, rows, head_dim, static_cast<__half *>(out));
+    combine_kernel<CKV_F16><<<blocks, 256, 0, st>>>(partials, parts, rows, head_dim, tpr,
+                                                    static_cast<__half *>(out));
   return cuda_status(cudaGetLastError());
 }
