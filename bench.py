@@ -60,6 +60,10 @@ def init_dist():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's communicator set-up lines (stderr) name the ranks and the
+        # transport each run used.
+        os.environ.setdefault('NCCL_DEBUG', 'INFO')
+        os.environ.setdefault('NCCL_DEBUG_SUBSYS', 'INIT')
         torch.cuda.set_device(local)
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device('cuda', local))
@@ -186,7 +190,16 @@ def algorithmic_bytes(view) -> int:
 
 
 class Sequence:
-    """8 layer caches of one sequence plus per-step inputs."""
+    """8 layer caches of one sequence plus per-step inputs.
+
+    The caches are built with ``update`` of 32767 tokens and then one decode
+    step (append + compaction), so the timed state starts right after a
+    compaction: 32640 packed tokens and a 128-token exact window, and the
+    first timed step attends over 32769 tokens.  Every ``ROLLBACK`` (128)
+    steps the layers return to that state; the compaction that the 128th step
+    of a cycle would do is therefore never timed inside the loop and is
+    charged separately (``compaction_seconds``).
+    """
 
     def __init__(self, seed, steps, device):
         from trpg_b200.quantized_kv import QuantizedAttentionLayer
@@ -199,9 +212,13 @@ class Sequence:
                 layer = QuantizedAttentionLayer(BITS)
                 layer.update(k, v)
                 del k, v
+                kn = torch.randn(1, HKV, 1, D, generator=gen, device=device).bfloat16()
+                layer.append_for_attention(kn, kn)
+                layer.compact_residual()
+                assert layer.keys.shape[2] == 128
                 self.layers.append(layer)
         torch.cuda.synchronize()
-        n = min(steps, ROLLBACK)
+        n = min(steps, ROLLBACK - 1)
         self.q = torch.randn(n, LAYERS, 1, HQ, 1, D, generator=gen, device=device).bfloat16()
         self.kn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
         self.vn = torch.randn(n, LAYERS, 1, HKV, 1, D, generator=gen, device=device).bfloat16()
@@ -214,29 +231,37 @@ class Sequence:
 
     @staticmethod
     def _snapshot(layer):
-        kb, vb = layer.key_bank, layer.value_bank
-        return (layer.keys, layer.values, layer.cumulative_length, kb.data, kb.meta, kb.units,
-                vb.data, vb.meta, vb.units)
+        # Every attribute of the layer and its banks (tensors by reference),
+        # as an append transaction keeps them: the in-place window's integers
+        # come back with its views, so appends after a rollback stay in place.
+        return dict(vars(layer)), dict(vars(layer.key_bank)), dict(vars(layer.value_bank))
 
     def rollback(self):
-        for layer, s in zip(self.layers, self.snap):
-            (layer.keys, layer.values, layer.cumulative_length, layer.key_bank.data,
-             layer.key_bank.meta, layer.key_bank.units, layer.value_bank.data,
-             layer.value_bank.meta, layer.value_bank.units) = s
+        for layer, (state, kb, vb) in zip(self.layers, self.snap):
+            vars(layer).clear()
+            vars(layer).update(state)
+            vars(layer.key_bank).clear()
+            vars(layer.key_bank).update(kb)
+            vars(layer.value_bank).clear()
+            vars(layer.value_bank).update(vb)
 
 
 def run_steps(seq, decode, steps, start=0, outs=None):
-    """Run ``steps`` decode steps (all layers); returns #kernel launches."""
+    """Run ``steps`` decode steps (all layers); returns #kernel launches.
+
+    A cycle is ROLLBACK - 1 steps from the snapshot (the window grows from
+    128 to 255 tokens, so no step compacts); then the layers roll back."""
     launches = 0
+    cycle = ROLLBACK - 1
     for s in range(start, start + steps):
-        i = s % ROLLBACK
+        i = s % cycle
         if i == 0 and s:
             seq.rollback()
         qs, kns, vns = seq.qs[i], seq.kns[i], seq.vns[i]
         for li, layer in enumerate(seq.layers):
             view = layer.append_for_attention(kns[li], vns[li])
             out = decode(qs[li], view, SCALE)
-            launches += 1
+            launches += 2
             units = layer.key_bank.units
             layer.compact_residual()
             launches += layer.key_bank.units != units
@@ -245,13 +270,39 @@ def run_steps(seq, decode, steps, start=0, outs=None):
     return launches
 
 
-def time_kernel(seq, decode, replays=32):
+def compaction_seconds(seq, repeats=8):
+    """Device seconds of one layer's compaction (quantize 128 tokens into the
+    banks and move the rest of the window), the work every 128th decode step
+    of a layer adds: each layer is brought to a 256-token window, compacted
+    between CUDA events, and rolled back."""
+    total, count = 0.0, 0
+    with torch.inference_mode():
+        for r in range(repeats):
+            for layer in seq.layers:
+                kn = seq.kn[0, 0].expand(1, HKV, 128, D).contiguous()
+                layer.append_for_attention(kn, kn)
+                assert layer.keys.shape[2] == 256
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                layer.compact_residual()
+                b.record()
+                b.synchronize()
+                if r:                       # the first round warms the allocator
+                    total += a.elapsed_time(b) * 1e-3
+                    count += 1
+            seq.rollback()
+    return total / count
+
+
+def time_kernel(seq, decode, min_seconds=0.6):
     """Mean device time of one decode launch.
 
     The 8 layers' decode launches (one token appended to each cache) are
     captured once in a CUDA graph and replayed back to back on one stream,
     between CUDA events on that stream, so host launch overhead is excluded;
-    the 8 distinct caches (591 MB) keep every launch reading from HBM.
+    the 8 distinct caches (591 MB) keep every launch reading from HBM.  The
+    replays run for at least ``min_seconds`` so that the clock sampler sees
+    the kernel under load.
     """
     with torch.inference_mode():
         views = [layer.append_for_attention(seq.kn[0, li], seq.vn[0, li])
@@ -267,21 +318,27 @@ def time_kernel(seq, decode, replays=32):
         with torch.cuda.graph(graph, stream=stream):
             for li, v in enumerate(views):
                 decode(seq.q[0, li], v, SCALE)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            graph.replay()
-            a.record(stream)
-            for _ in range(replays):
+
+        def replay(n):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
                 graph.replay()
-            b.record(stream)
-        stream.synchronize()
-        sec = a.elapsed_time(b) * 1e-3 / (replays * LAYERS)
+                a.record(stream)
+                for _ in range(n):
+                    graph.replay()
+                b.record(stream)
+            stream.synchronize()
+            return a.elapsed_time(b) * 1e-3
+
+        probe = replay(32) / 32
+        replays = max(32, int(min_seconds / probe) + 1)
+        sec = replay(replays) / (replays * LAYERS)
         del graph
     seq.rollback()
-    return sec, statistics.mean(sizes)
+    return sec, statistics.mean(sizes), replays
 
 
-def cpu_reference(steps, warmup, sample_layers=1):
+def cpu_reference(steps, warmup, one_thread_steps=0):
     """The reference CPU path on one layer per step (a bounded sample)."""
     from oracle import ckv_cpu_path as P
     threads = os.cpu_count() or 1
@@ -294,21 +351,33 @@ def cpu_reference(steps, warmup, sample_layers=1):
     snap = (layer.keys, layer.values, layer.length, layer.kd, layer.km, layer.vd, layer.vm)
     q = torch.randn(1, HQ, 1, D, generator=gen).bfloat16()
     kn = torch.randn(1, HKV, 1, D, generator=gen).bfloat16()
+    def timed(n):
+        times = []
+        for i in range(n):
+            if i and i % ROLLBACK == 0:
+                layer.keys, layer.values, layer.length, layer.kd, layer.km, layer.vd, layer.vm = snap
+            t = time.perf_counter()
+            P.decode_step(layer, q, kn, kn, SCALE)
+            times.append(time.perf_counter() - t)
+        return statistics.mean(times)
+
     for i in range(warmup):
         P.decode_step(layer, q, kn, kn, SCALE)
-    times = []
-    for i in range(steps):
-        if i and i % ROLLBACK == 0:
-            layer.keys, layer.values, layer.length, layer.kd, layer.km, layer.vd, layer.vm = snap
-        t = time.perf_counter()
-        P.decode_step(layer, q, kn, kn, SCALE)
-        times.append(time.perf_counter() - t)
-    per_layer = statistics.mean(times)
-    return {'value': 1.0 / (LAYERS * per_layer), 'unit': 'tok/s', 'cores': threads,
-            'kind': 'port', 'ms_per_layer': per_layer * 1e3,
-            'sample': f'{steps} decode steps of 1 of the 8 identical 32K-token Q8 layers '
-                      f'(append + dequantize + SDPA + compact), torch CPU ops, {threads} threads; '
-                      f'tok/s = 1 / (8 x mean layer time)'}
+    per_layer = timed(steps)
+    out = {'value': 1.0 / (LAYERS * per_layer), 'unit': 'tok/s', 'cores': threads,
+           'kind': 'port', 'ms_per_layer': per_layer * 1e3,
+           'sample': f'{steps} decode steps of 1 of the 8 identical 32K-token Q8 layers '
+                     f'(append + dequantize + SDPA + compact), torch CPU ops, {threads} threads; '
+                     f'tok/s = 1 / (8 x mean layer time)'}
+    if one_thread_steps:
+        torch.set_num_threads(1)
+        try:
+            single = timed(one_thread_steps)
+        finally:
+            torch.set_num_threads(threads)
+        out['one_thread'] = {'value': 1.0 / (LAYERS * single), 'unit': 'tok/s', 'cores': 1,
+                             'ms_per_layer': single * 1e3, 'sample': f'{one_thread_steps} decode steps'}
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -330,12 +399,15 @@ def reference_arm(args, world, rank):
 
 
 def config(args, world):
-    return {'workload': 'single-sequence Q8 decode, 8 layers x 32K context (32512 packed + 256 '
-                        'bf16 recent), 16q/4kv x 256, append-quantize + decode per layer',
+    return {'workload': 'single-sequence Q8 decode, 8 layers x 32K context (32640 packed + '
+                        '129..255 bf16 recent tokens: 32769..32895 in all), 16q/4kv x 256, '
+                        'append + decode per layer; the 128-token compaction every 128 steps '
+                        'is timed separately and charged per step',
             'model': 'attention only (no weights)', 'global_batch': world, 'seq_len': CONTEXT,
             'parallelism': f'dp{world} (independent sequences)', 'layers': LAYERS,
             'heads_q': HQ, 'heads_kv': HKV, 'head_dim': D, 'bits': BITS,
-            'l2': 'inputs larger than L2 (8 distinct caches, 591 MB per GPU)'}
+            'l2': 'inputs larger than L2 (8 distinct caches, 591 MB per GPU)',
+            'clocks_window': 'the timed loop plus the roofline replays (at least 0.6 s)'}
 
 
 def b200_arm(args, world, rank, local):
@@ -362,41 +434,14 @@ def b200_arm(args, world, rank, local):
     stop.record()
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
+    barrier(world)
+    loop_ms = max_over_ranks(start.elapsed_time(stop), world)
+    seq.rollback()
+
+    # ---- roofline of the decode kernel (the clock window extends over it) ----
+    sec, bytes_per_launch, replays = time_kernel(seq, decode)
     clocks.stop()
-    barrier(world)
-    ms = max_over_ranks(start.elapsed_time(stop), world)
-    seq.rollback()
-
-    # ---- end to end through the public API with host buffers -----------------
-    pin = lambda t: t.cpu().pin_memory()
-    hq, hk, hv = pin(seq.q), pin(seq.kn), pin(seq.vn)
-    host_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
-    from trpg_b200.compressed_kv_attention import compressed_kv_decode
-    outs = [None] * LAYERS
-    e2e_steps = args.steps
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for s in range(e2e_steps):
-        i = s % ROLLBACK
-        if i == 0 and s:
-            seq.rollback()
-        q = hq[i].to(device, non_blocking=True).unbind(0)
-        kn = hk[i].to(device, non_blocking=True).unbind(0)
-        vn = hv[i].to(device, non_blocking=True).unbind(0)
-        with torch.inference_mode():
-            for li, layer in enumerate(seq.layers):
-                view = layer.append_for_attention(kn[li], vn[li])
-                outs[li] = compressed_kv_decode(q[li], view, SCALE)
-                layer.compact_residual()
-        host_out.copy_(torch.stack(outs))   # blocking read of the step's result
-    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
-    seq.rollback()
-    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
-    d2h = host_out.numel() * 2
-
-    # ---- roofline of the decode kernel -----------------------------------------
-    sec, bytes_per_launch = time_kernel(seq, decode)
+    sec = max_over_ranks(sec, world)
     peak, peak_kind = peaks()
     achieved = bytes_per_launch / sec / 1e9
     traffic = None
@@ -404,31 +449,90 @@ def b200_arm(args, world, rank, local):
     if tfile.exists():
         traffic = json.loads(tfile.read_text()).get('bytes_per_launch')
 
-    us_step = ms * 1e3 / args.steps
-    value = world * args.steps / (ms * 1e-3)
+    # ---- the compaction every 128th step adds, charged per step -------------
+    compact_s = max_over_ranks(compaction_seconds(seq), world)
+    amortised_ms = LAYERS * compact_s * 1e3 / ROLLBACK
+    ms = loop_ms / args.steps + amortised_ms          # per step
+
+    # ---- end to end through the public API with host buffers -----------------
+    e2e = e2e_run(seq, args, world, device)
+    e2e_ms = e2e['ms'] + amortised_ms
+
+    value = world / (ms * 1e-3)
     line = {'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': world,
-            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms / args.steps,
-            'us_per_step': us_step, 'us_per_layer': us_step / LAYERS,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'us_per_step': ms * 1e3, 'us_per_layer': ms * 1e3 / LAYERS,
+            'us_per_step_loop': loop_ms * 1e3 / args.steps,
+            'compaction_us_per_layer': compact_s * 1e6,
             'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'u8/bf16', 'data': 'synthetic (seeded N(0,1), 1% outlier channels x8)',
             'config': config(args, world),
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
                          'frac': achieved / peak, 'traffic': traffic, 'peak_source': peak_kind,
                          'kernel': 'attn_kernel<8,256,1,bf16>',
-                         'bytes_per_launch': bytes_per_launch, 'us_per_launch': sec * 1e6},
-            'hbm_gbs_step': world * LAYERS * bytes_per_launch * args.steps / (ms * 1e-3) / 1e9 / world,
+                         'bytes_per_launch': bytes_per_launch, 'us_per_launch': sec * 1e6,
+                         'launches_timed': replays * LAYERS},
+            'hbm_gbs_step': LAYERS * bytes_per_launch / (ms * 1e-3) / 1e9,
             'clocks': clocks.summary(),
-            'e2e': {'value': world * e2e_steps / (e2e_ms * 1e-3), 'unit': 'tok/s',
-                    'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
-                    'us_per_step': e2e_ms * 1e3 / e2e_steps},
+            'e2e': {'value': world / (e2e_ms * 1e-3), 'unit': 'tok/s',
+                    'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
+                    'us_per_step': e2e_ms * 1e3},
             'gpu_launches': launches}
+    del seq
+    torch.cuda.empty_cache()
+    # The partitionings the multi-GPU path is built for, at every N.
+    line['batch_sharded'] = measure_extra('c3', args, world, rank, device)
+    line['split_kv'] = measure_extra('c5', args, world, rank, device)
     if rank == 0 and world == 1 and not args.no_cpu:
-        del seq
         torch.cuda.empty_cache()
-        base = cpu_reference(args.cpu_steps, 1)
+        base = cpu_reference(args.cpu_steps, 1, one_thread_steps=args.cpu_one_thread_steps)
         line['cpu_baseline'] = {k: base[k] for k in ('value', 'unit', 'cores', 'kind', 'sample')}
+        if 'one_thread' in base:
+            line['cpu_baseline']['one_thread'] = base['one_thread']
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def e2e_run(seq, args, world, device):
+    """The decode step through the public API (``compressed_kv_decode``), with
+    the step's query and new key/value rows copied from pinned host memory
+    and the 8 outputs read back to host memory every step; warmed up, then
+    ``args.steps`` steps timed (wall clock around a synchronised loop, max
+    over ranks)."""
+    from trpg_b200.compressed_kv_attention import compressed_kv_decode
+    n = seq.q.shape[0]
+    # One pinned buffer per step: q, k, v of all layers back to back.
+    parts = (seq.q, seq.kn, seq.vn)
+    flat = torch.cat([t.reshape(n, -1) for t in parts], 1).cpu().pin_memory()
+    sizes = [t[0].numel() for t in parts]
+    shapes = [t.shape[1:] for t in parts]
+    host_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
+    outs = [None] * LAYERS
+    cycle = ROLLBACK - 1
+
+    def steps(count):
+        for s in range(count):
+            i = s % cycle
+            if i == 0 and s:
+                seq.rollback()
+            dev = flat[i].to(device, non_blocking=True)
+            q, kn, vn = (x.view(shape).unbind(0) for x, shape in zip(dev.split(sizes), shapes))
+            with torch.inference_mode():
+                for li, layer in enumerate(seq.layers):
+                    view = layer.append_for_attention(kn[li], vn[li])
+                    outs[li] = compressed_kv_decode(q[li], view, SCALE)
+                    layer.compact_residual()
+                host_out.copy_(torch.stack(outs))   # blocking read of the step's result
+
+    steps(max(3, args.warmup))
+    seq.rollback()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    steps(args.steps)
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+    seq.rollback()
+    return {'ms': e2e_ms / args.steps, 'h2d': flat[0].numel() * 2, 'd2h': host_out.numel() * 2}
 
 
 # ---------------------------------------------------------------------------
@@ -494,17 +598,20 @@ def graph_seconds(fn, replays=20):
     return a.elapsed_time(b) * 1e-3 / replays
 
 
-def extra_workload(args, world, rank, local):
-    from trpg_b200 import _native
+def measure_extra(w, args, world, rank, device, min_steps=20):
+    """One of the other configurations at ``world`` GPUs, as a dict.
+
+    c3 / c4: the sequences are sharded over the ranks by LPT on bytes and
+    each rank runs one launch over its share (no collective); c5: each rank
+    computes the (o, m, l) partial of its contiguous share of the 131072-token
+    history, the partials are all-gathered over NCCL and merged.  Kernel time
+    comes from CUDA-graph replays of one launch; the step (for c5 on several
+    GPUs: partial, all-gather and merge, each between CUDA events) is timed
+    over at least ``min_steps`` steps; every figure is the max over ranks."""
     from trpg_b200.compressed_kv_kernels import attention, combine
     from trpg_b200.sharding import lpt_partition, split_kv_range, view_bytes
-    _native.load()
-    device = torch.device('cuda', local)
-    torch.cuda.set_device(device)
     gen = torch.Generator(device=device)
     peak, peak_kind = peaks()
-    w = args.workload
-    clocks = Clocks(local)
     if w in ('c3', 'c4'):
         if w == 'c3':
             cpu = torch.Generator().manual_seed(3)
@@ -543,42 +650,71 @@ def extra_workload(args, world, rank, local):
     else:
         raise SystemExit(f'unknown workload {w}')
     sec_kernel = graph_seconds(fn)
-    # Whole step (for c5 on several GPUs: partial + NCCL all-gather + merge),
-    # device-timed over the steps, max over ranks.
-    if w == 'c5' and world > 1:
+    steps = max(min_steps, args.steps)
+    exchange = w == 'c5' and world > 1
+    if exchange:
         import torch.distributed as dist
-        def step():
-            part = fn()[0]
-            out = torch.empty((world * part.shape[0], part.shape[1]), dtype=part.dtype, device=device)
-            dist.all_gather_into_tensor(out, part)
-            return combine(out.view(world, *part.shape), torch.bfloat16)
-    else:
-        step = fn
+        gathered = None
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     with torch.inference_mode():
-        for _ in range(args.warmup):
+        def step(e=None):
+            nonlocal gathered
+            if e:
+                e[0].record()
+            out = fn()
+            if exchange:
+                part = out[0]
+                if e:
+                    e[1].record()
+                if gathered is None:
+                    gathered = torch.empty((world * part.shape[0], part.shape[1]), dtype=part.dtype,
+                                           device=device)
+                dist.all_gather_into_tensor(gathered, part)
+                out = combine(gathered.view(world, *part.shape), torch.bfloat16)
+            if e:
+                e[2].record()
+            return out
+        for _ in range(max(3, args.warmup)):
             step()
         torch.cuda.synchronize()
         barrier(world)
-        clocks.start()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(args.steps):
-            step()
+        for i in range(steps):
+            step(ev[i] if exchange else None)
         b.record()
         torch.cuda.synchronize()
-        clocks.stop()
         barrier(world)
-    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world)
+    ms = max_over_ranks(a.elapsed_time(b) / steps, world)
     k_us = max_over_ranks(sec_kernel * 1e6, world)
     achieved = nbytes / sec_kernel / 1e9
-    line = {'metric': f'{w}: decode attention tokens/s', 'workload': WORKLOADS[w], 'value': tokens / (ms * 1e-3),
-            'unit': 'tok/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
-            'ms_per_step': ms, 'higher_is_better': True,
-            'scaling': 'strong' if w == 'c5' else 'strong (fixed batch sharded)',
-            'dtype': 'u4/bf16' if w == 'c5' else 'u8/bf16', 'data': 'synthetic',
-            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
-                         'frac': achieved / peak, 'peak_source': peak_kind,
-                         'bytes_per_launch_rank0': nbytes, 'us_per_launch_max_rank': k_us},
+    out = {'workload': WORKLOADS[w], 'value': tokens / (ms * 1e-3), 'unit': 'tok/s',
+           'n_gpus': world, 'steps': steps, 'ms_per_step': ms,
+           'scaling': 'strong' if w == 'c5' else 'strong (fixed batch sharded)',
+           'dtype': 'u4/bf16' if w == 'c5' else 'u8/bf16',
+           'roofline': {'bound': 'hbm', 'achieved_rank0': achieved, 'peak': peak, 'unit': 'GB/s',
+                        'frac_rank0': achieved / peak, 'peak_source': peak_kind,
+                        'bytes_per_launch_rank0': nbytes, 'us_per_launch_max_rank': k_us}}
+    if exchange:
+        compute = statistics.median(e[0].elapsed_time(e[1]) for e in ev) * 1e3
+        combine_us = statistics.median(e[1].elapsed_time(e[2]) for e in ev) * 1e3
+        out['us_partial_max_rank'] = max_over_ranks(compute, world)
+        out['us_allgather_combine_max_rank'] = max_over_ranks(combine_us, world)
+    return out
+
+
+def extra_workload(args, world, rank, local):
+    from trpg_b200 import _native
+    _native.load()
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    clocks = Clocks(local)
+    clocks.start()
+    line = measure_extra(args.workload, args, world, rank, device)
+    clocks.stop()
+    line = {'metric': f'{args.workload}: decode attention tokens/s', **line,
+            'warmup': args.warmup, 'higher_is_better': True, 'data': 'synthetic',
             'clocks': clocks.summary()}
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -647,6 +783,7 @@ def main():
     ap.add_argument('--warmup', type=int, default=16)
     ap.add_argument('--impl', choices=('b200', 'reference'), default='b200')
     ap.add_argument('--cpu-steps', type=int, default=24)
+    ap.add_argument('--cpu-one-thread-steps', type=int, default=3)
     ap.add_argument('--no-cpu', action='store_true')
     ap.add_argument('--workload', choices=('c2',) + tuple(WORKLOADS), default='c2',
                     help='c2 (default) is the headline 32K decode step; c3/c4/c5 measure the '

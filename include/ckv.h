@@ -179,7 +179,10 @@ int ckv_attention_workspace(const ckv_attn_args *args, size_t *bytes);
 
 /* Copy the workspace's error word to *flag and wait for the stream: 0, or 1
  * when a kernel gave up waiting for an asynchronous copy (about a second)
- * instead of hanging.  The word stays set until the caller clears it. */
+ * instead of hanging.  The word stays set until the caller clears it.
+ * workspace == NULL reads the word of the current device's static scratch
+ * array instead (see ckv_attention_static; every static call clears it
+ * before its kernel runs, so it reports the latest static call). */
 int ckv_attention_error(const void *workspace, int *flag, ckv_stream_t stream);
 
 /*
@@ -216,8 +219,11 @@ int ckv_attention(const ckv_attn_args *args, void *workspace, size_t workspace_b
  * that device current; make that first call before any stream capture.
  * Every call on one device uses the same array: two calls whose kernels can
  * overlap on the GPU (different streams without ordering between them) race
- * and give wrong results, so the caller must serialise them.  The give-up
- * flag that ckv_attention_error reads is not exposed for this array.
+ * and give wrong results, so the caller must serialise them.  A bounded wait
+ * that gave up inside the kernel is reported by
+ * ckv_attention_error(NULL, &flag, stream) for this array.  The array's
+ * address is cached per device and CUDA context, so a cudaDeviceReset is
+ * followed by a fresh lookup on the next call.
  * No counterpart in the reference.
  */
 int ckv_attention_static(const ckv_attn_args *args, ckv_stream_t stream);

@@ -241,6 +241,34 @@ class OracleLayer:
         self.compact_residual()
         return keys, values
 
+    def fill(self, k: np.ndarray, v: np.ndarray):
+        """The state ``update`` leaves (append, then compact) without
+        dequantizing the history, for long contexts whose dequantized copy
+        would not fit in memory."""
+        self.append_for_attention(k, v)
+        self.compact_residual()
+
+    def head_kv(self, head: int, t0: int, t1: int, fused: bool = True):
+        """Keys and values [t1 - t0, D] of one KV head for absolute positions
+        [t0, t1): dequantized packed tokens, then the exact window."""
+        parts_k, parts_v = [], []
+        p = self.packed_tokens
+        if t0 < p:
+            a, b = t0, min(t1, p)
+            u0, u1 = a // 128, -(-b // 128)
+            kh = unpack_key_bank(self.kd[:, head:head + 1, u0:u1], self.km[:, head:head + 1, u0:u1],
+                                 self.bits, self.dtype, fused)[0, 0]
+            vh = unpack_value_bank(self.vd[:, head:head + 1, u0 * 128:u1 * 128],
+                                   self.vm[:, head:head + 1, u0 * 128:u1 * 128],
+                                   self.bits, self.dtype, fused)[0, 0]
+            parts_k.append(kh[a - u0 * 128:b - u0 * 128])
+            parts_v.append(vh[a - u0 * 128:b - u0 * 128])
+        if t1 > p:
+            a, b = max(t0, p) - p, t1 - p
+            parts_k.append(self.keys[0, head, a:b])
+            parts_v.append(self.values[0, head, a:b])
+        return np.concatenate(parts_k, 0), np.concatenate(parts_v, 0)
+
 
 # --------------------------------------------------------------------------
 # Attention (restated SDPA with GQA and a lower-right causal mask)
@@ -277,6 +305,54 @@ def decode_reference(q: np.ndarray, layer: OracleLayer, scale: float, fused: boo
     if causal_lower_right is None:
         causal_lower_right = q.shape[2] > 1
     return attention(q, keys, values, scale, causal_lower_right)
+
+
+def decode_reference_chunked(q: np.ndarray, layer: OracleLayer, scale: float, fused: bool = True,
+                             causal_lower_right: bool | None = None, chunk: int = 8192,
+                             t0: int = 0, t1: int | None = None):
+    """``decode_reference`` with bounded memory: one KV head and ``chunk``
+    positions at a time, softmax merged across chunks in float64 (the same
+    log-sum-exp rule as ``combine_partials``).
+
+    With ``t0`` / ``t1`` it covers only positions [t0, t1) and returns the
+    unnormalised (m, l, o) of that range in the log2 domain instead (the
+    split-KV partial of a shard).  Query row i of n may see position j iff
+    j <= L - n + i when ``causal_lower_right``.
+    """
+    b, hq, n, d = q.shape
+    length = layer.length
+    if causal_lower_right is None:
+        causal_lower_right = n > 1
+    partial = t1 is not None
+    t1 = length if t1 is None else t1
+    heads = layer.kd.shape[1] if layer.kd is not None else layer.keys.shape[1]
+    group = hq // heads
+    log2e = np.log2(np.e)
+    m = np.full((hq, n), -np.inf)
+    l = np.zeros((hq, n))
+    o = np.zeros((hq, n, d))
+    for h in range(heads):
+        qh = q[0, h * group:(h + 1) * group].astype(np.float64).reshape(group * n, d)
+        rows = np.arange(group * n) % n
+        for a in range(t0, t1, chunk):
+            e = min(t1, a + chunk)
+            kh, vh = layer.head_kv(h, a, e, fused)
+            s2 = (qh @ kh.astype(np.float64).T) * (scale * log2e)
+            if causal_lower_right:
+                pos = np.arange(a, e)[None, :]
+                s2 = np.where(pos <= length - n + rows[:, None], s2, -np.inf)
+            mm = m[h * group:(h + 1) * group].reshape(-1)
+            mc = np.maximum(mm, s2.max(-1))
+            safe = np.where(np.isfinite(mc), mc, 0.0)
+            alpha = np.where(np.isfinite(mm), np.exp2(mm - safe), 0.0)
+            p = np.where(np.isfinite(s2), np.exp2(s2 - safe[:, None]), 0.0)
+            sl = slice(h * group, (h + 1) * group)
+            l[sl] = (l[sl].reshape(-1) * alpha + p.sum(-1)).reshape(group, n)
+            o[sl] = (o[sl].reshape(-1, d) * alpha[:, None] + p @ vh.astype(np.float64)).reshape(group, n, d)
+            m[sl] = mc.reshape(group, n)
+    if partial:
+        return m[None], l[None], o[None]
+    return (o / l[..., None])[None]
 
 
 # --------------------------------------------------------------------------
@@ -345,6 +421,9 @@ def cache_state(seed: int, heads: int, length: int, dim: int, bits: int, new_tok
             k[:, h, :, idx[h]] = round_to(k[:, h, :, idx[h]] * 8, dtype)
             v[:, h, :, idx[h]] = round_to(v[:, h, :, idx[h]] * 8, dtype)
     layer = OracleLayer(bits, rounding, dtype)
-    layer.update(k[:, :, :length - new_tokens], v[:, :, :length - new_tokens])
+    if length > 16384:
+        layer.fill(k[:, :, :length - new_tokens], v[:, :, :length - new_tokens])
+    else:
+        layer.update(k[:, :, :length - new_tokens], v[:, :, :length - new_tokens])
     layer.append_for_attention(k[:, :, length - new_tokens:], v[:, :, length - new_tokens:])
     return layer, k, v

@@ -36,6 +36,10 @@ def test_cpu_inputs_return_none_so_callers_fall_back():
 def test_only_lower_right_causal_masks_are_eligible():
     from torch.nn.attention.bias import causal_lower_right, causal_upper_left
     assert _supported_mask(None, 512)
+    # Several queries without a mask: upstream aligns its causal mask top-left,
+    # which the kernels do not reproduce, so the call stays upstream.
+    assert not _supported_mask(None, 512, 2)
+    assert not _supported_mask(None, 512, 64)
     assert _supported_mask(causal_lower_right(1, 512), 512)
     assert not _supported_mask(causal_upper_left(1, 512), 512)
     assert not _supported_mask(causal_lower_right(2, 512), 512)
@@ -128,3 +132,94 @@ def test_split_kv_exchange_over_gloo_matches_full_attention(world):
         assert p.exitcode == 0
     assert len(result) == world
     assert max(result.values()) < 1e-5
+
+
+FAKE_SCOPE = """
+from contextlib import contextmanager
+from contextvars import ContextVar
+_MTP_VERIFICATION_ENABLED = ContextVar('fake_flag', default=False)
+@contextmanager
+def mtp_verification_scope(enabled=True):
+    token = _MTP_VERIFICATION_ENABLED.set(bool(enabled))
+    try:
+        yield
+    finally:
+        _MTP_VERIFICATION_ENABLED.reset(token)
+"""
+FAKE_CACHE = """
+class QuantizedAttentionLayer:
+    pass
+def make_cache(config, mode='q8'):
+    return 'reference cache'
+def cache_bytes(cache):
+    return -1
+"""
+FAKE_CALLER = """
+from .quantized_kv import make_cache, cache_bytes, QuantizedAttentionLayer
+from .mtp_verification_kernels import mtp_verification_scope
+"""
+
+
+def test_install_routes_every_module_and_shares_the_verify_flag(tmp_path, monkeypatch):
+    """A package laid out like the reference: a caller imported before
+    install() gets this package's functions and classes, one imported after
+    gets them through the module table, and the caller's verify scope turns
+    on the flag the patched forward reads."""
+    import importlib
+    import sys
+    from trpg_b200 import install as I
+    from trpg_b200 import compressed_kv_attention as A
+    from trpg_b200 import mtp_verification_kernels as S
+    from trpg_b200 import quantized_kv as Q
+    pkg = tmp_path / 'fakeref'
+    pkg.mkdir()
+    (pkg / '__init__.py').write_text('')
+    (pkg / 'mtp_verification_kernels.py').write_text(FAKE_SCOPE)
+    (pkg / 'quantized_kv.py').write_text(FAKE_CACHE)
+    (pkg / 'early_caller.py').write_text(FAKE_CALLER)
+    (pkg / 'late_caller.py').write_text(FAKE_CALLER)
+    monkeypatch.syspath_prepend(str(tmp_path))
+    own_flag = S._MTP_VERIFICATION_ENABLED
+    early = importlib.import_module('fakeref.early_caller')
+    assert early.make_cache(None) == 'reference cache'
+    try:
+        I.install('fakeref')
+        assert sys.modules['fakeref.quantized_kv'] is Q
+        for name in I.MODULES:
+            assert sys.modules[f'fakeref.{name}'].__name__ == f'trpg_b200.{name}'
+        assert early.make_cache is Q.make_cache and early.cache_bytes is Q.cache_bytes
+        assert early.QuantizedAttentionLayer is Q.QuantizedAttentionLayer
+        late = importlib.import_module('fakeref.late_caller')
+        assert late.make_cache is Q.make_cache
+        for scope in (early.mtp_verification_scope, late.mtp_verification_scope):
+            assert not A._scope.mtp_verification_enabled()
+            with scope():
+                assert A._scope.mtp_verification_enabled()
+            assert not A._scope.mtp_verification_enabled()
+    finally:
+        I.uninstall('fakeref')
+        S.bind(own_flag)
+        for name in list(sys.modules):
+            if name == 'fakeref' or name.startswith('fakeref.'):
+                del sys.modules[name]
+
+
+def test_layer_state_is_what_a_cache_transaction_can_snapshot():
+    """The reference transaction (models/hybrid_cache_transaction.py:74-99)
+    keeps tensors of a quantized layer only under keys / values (by
+    reference) and the banks' data / meta; every other attribute must be
+    plain metadata.  The in-place window therefore lives in integers."""
+    from trpg_b200.quantized_kv import QuantizedAttentionLayer
+    plain = (bool, int, float, str, torch.dtype, torch.device, type, type(None))
+    layer = QuantizedAttentionLayer(8)
+    x = torch.zeros(1, 2, 5, 64, dtype=torch.bfloat16)
+    with torch.inference_mode():
+        layer.append_for_attention(x, x)        # CPU tensors: the concatenating path
+    for name, value in vars(layer).items():
+        if name in ('keys', 'values'):
+            assert isinstance(value, torch.Tensor)
+        elif name in ('key_bank', 'value_bank'):
+            for bname, bvalue in vars(value).items():
+                assert bname in ('data', 'meta') or isinstance(bvalue, plain), bname
+        else:
+            assert isinstance(value, plain), (name, type(value))

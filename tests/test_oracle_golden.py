@@ -96,3 +96,30 @@ def test_cpu_timing_path_matches_reference(name):
     q = torch.from_numpy(O.seeded_normal(seed + 2, (1, hq, n, dim), dtype)).to(tdt)
     out = P.attend(q, layer, float(A[f'{name}_scale'])).float().numpy()
     np.testing.assert_array_equal(out, A[f'{name}_output'])
+
+
+@pytest.mark.parametrize('bits,nq,length', [(8, 1, 3000), (4, 4, 1500), (8, 3, 700)])
+def test_chunked_oracle_equals_the_whole_history_oracle(bits, nq, length):
+    """The bounded-memory attention used at full sizes agrees with the
+    dequantize + cat + SDPA restatement, whole and as merged shards."""
+    layer, _, _ = O.cache_state(31 + bits, 2, length, 64, bits, new_tokens=nq)
+    q = O.seeded_normal(37, (1, 6, nq, 64))
+    want = O.decode_reference(q, layer, .125)
+    got = O.decode_reference_chunked(q, layer, .125, chunk=256)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-12)
+    if nq == 1:
+        cut = [0, 1024, 1300, layer.length]
+        parts = [O.decode_reference_chunked(q, layer, .125, chunk=200, t0=a, t1=b)
+                 for a, b in zip(cut, cut[1:])]
+        merged = O.combine_partials(*zip(*parts))
+        np.testing.assert_allclose(merged, want, rtol=0, atol=1e-12)
+
+
+def test_fill_leaves_the_state_update_leaves():
+    k = O.seeded_normal(41, (1, 2, 900, 64))
+    v = O.seeded_normal(42, (1, 2, 900, 64))
+    a, b = O.OracleLayer(8), O.OracleLayer(8)
+    a.update(k, v)
+    b.fill(k, v)
+    assert O.digest(a.kd, a.km, a.vd, a.vm, a.keys, a.values) == \
+        O.digest(b.kd, b.km, b.vd, b.vm, b.keys, b.values)

@@ -116,6 +116,20 @@ def test_static_matches_workspace_entry_twice(bits, nq, lengths):
         e = e.float().cpu().numpy()
         np.testing.assert_allclose(a.float().cpu().numpy(), e, rtol=RTOL, atol=ATOL)
         np.testing.assert_allclose(b.float().cpu().numpy(), e, rtol=RTOL, atol=ATOL)
+    assert _static_gave_up() == 0
+
+
+def _static_gave_up():
+    """The static array's give-up word, read through ckv_attention_error with
+    no workspace (0: no bounded wait of the last static call ran out)."""
+    lib = _native.library()
+    lib.ckv_attention_error.argtypes = [VP, ctypes.POINTER(ctypes.c_int), VP]
+    lib.ckv_attention_error.restype = ctypes.c_int
+    flag = ctypes.c_int(-1)
+    rc = lib.ckv_attention_error(None, ctypes.byref(flag),
+                                 VP(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, lib.ckv_last_error()
+    return flag.value
 
 
 @pytest.mark.gpu

@@ -2,16 +2,18 @@
 
 Mirror of ``models/compressed_kv_attention.py`` over the B200 kernels:
 
-* ``compressed_kv_decode(query, view, scale)`` -- the same eligibility guard
-  as the reference (``:8-29``); returns ``None`` for anything the kernel does
-  not cover so the caller falls back to SDPA.
+* ``compressed_kv_decode(query, view, scale)`` -- the same eligibility rules
+  as the reference (``:8-29``), applied in C++ in the same op call as the
+  kernel; returns ``None`` for anything the kernel does not cover so the
+  caller falls back to SDPA.
 * ``compressed_kv_verify(query, view, scale)`` -- new: the multi-query
-  (MTP verify) variant, 2..16 query rows per KV head, lower-right causal.
+  (MTP verify) variant, up to 16 query rows per KV head, lower-right causal.
 * ``_supported_mask`` (``:32-37``), ``_forward`` (``:40-82``),
   ``configure_compressed_kv_attention`` (``:85-95``) and
   ``compressed_kv_info`` (``:98-103``).  ``_forward`` additionally routes
   2..4-token calls to ``compressed_kv_verify`` inside
-  ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``), and
+  ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``, which
+  shares the reference's flag once ``trpg_b200.install`` has run), and
   chunks over a packed history to ``compressed_kv_prefill``
   (``trpg_b200.compressed_prefill_attention``): 16..1024 tokens by default,
   where the packed kernel is faster than dequantize + SDPA, up to 4096 with
@@ -22,85 +24,81 @@ Kernel launch errors raise; only "unsupported" returns ``None``.
 """
 from __future__ import annotations
 
-import math
+import sys
 from types import MethodType
 
 import torch
 
-from .mtp_verification_kernels import mtp_verification_enabled
+from . import mtp_verification_kernels as _scope
 from .quantized_kv import QuantizedAttentionLayer
 
 BACKEND = 'b200-affine-q4-q8-cuda'
 
 
-def _view_ok(query, view, min_residual):
-    if view.bits not in (4, 8) or not math.isfinite(view.length):
+DECODE_ROUTE, VERIFY_ROUTE = 0, 1   # Route in trpg_b200/csrc/ckv_torch.cpp
+
+_guarded_ops = {}
+
+
+def _quantized_layer(layer):
+    """This package's cache layer, or the reference's own (``models.quantized_kv``
+    loaded before ``install()`` ran): both hand out the same view and keep
+    the same layout, so the kernels serve either."""
+    if isinstance(layer, QuantizedAttentionLayer):
+        return True
+    cls = type(layer)
+    if cls.__name__ != 'QuantizedAttentionLayer':
         return False
-    tensors = (view.keys, view.values, view.key_data, view.key_meta, view.value_data, view.value_meta)
-    if any(t is None or t.device != query.device or t.requires_grad for t in tensors):
-        return False
-    if (view.keys.ndim != 4 or view.values.shape != view.keys.shape or view.keys.shape[0] != 1
-            or view.keys.dtype != query.dtype or view.values.dtype != query.dtype
-            or view.keys.shape[-1] != query.shape[-1] or query.shape[1] % view.keys.shape[1]
-            or view.length != view.packed_tokens + view.keys.shape[2]
-            or view.keys.shape[2] < min_residual
-            or view.keys.stride(-1) != 1 or view.values.stride(-1) != 1):
-        return False
-    return True
+    module = sys.modules.get(cls.__module__)
+    return getattr(module, 'QuantizedAttentionLayer', None) is cls and hasattr(layer, 'key_bank')
 
 
-def _query_ok(query, scale):
-    return (query.is_cuda and not torch.is_grad_enabled() and not torch.is_autocast_enabled('cuda')
-            and query.ndim == 4 and query.shape[0] == 1
-            and query.dtype in (torch.bfloat16, torch.float16) and query.stride(-1) == 1
-            and query.shape[-1] in (64, 128, 256) and not query.requires_grad
-            and math.isfinite(scale))
-
-
-_guarded_op = None
-
-
-def compressed_kv_decode(query, view, scale):
-    """Single-query decode, or None when unsupported (reference ``:8-29``).
-
-    One op call (``torch.ops.ckv.decode_guarded``) applies the guard of
-    ``_query_ok`` / ``_view_ok`` in C++ and runs the kernel when it passes.
-    """
-    global _guarded_op
+def _run_guarded(query, view, scale, route):
+    """The view's plain fields are type-checked here; the acceptance rules of
+    the kernels (the reference's guard, ``:8-29``) and the launch run in one
+    C++ op call, which returns None when the call is not covered."""
     length, bits, packed = view.length, view.bits, view.packed_tokens
     if (type(length) is not int or type(packed) is not int or type(bits) is not int
             or not isinstance(scale, (int, float)) or isinstance(scale, bool)):
         return None
-    if _guarded_op is None:
+    op = _guarded_ops.get(route)
+    if op is None:
         from ._native import ops
-        _guarded_op = ops().decode_guarded
-    return _guarded_op(query, view.key_data, view.key_meta, view.value_data, view.value_meta,
-                       view.keys, view.values, packed, length, bits, float(scale))
+        op = _guarded_ops[route] = (ops().decode_guarded if route == DECODE_ROUTE
+                                    else ops().attention_guarded)
+    if route == DECODE_ROUTE:
+        return op(query, view.key_data, view.key_meta, view.value_data, view.value_meta,
+                  view.keys, view.values, packed, length, bits, float(scale))
+    return op(query, view.key_data, view.key_meta, view.value_data, view.value_meta,
+              view.keys, view.values, packed, length, bits, float(scale), route)
+
+
+def compressed_kv_decode(query, view, scale):
+    """Single-query decode over a packed view, or None when unsupported
+    (reference ``:8-29``); launch errors raise."""
+    return _run_guarded(query, view, scale, DECODE_ROUTE)
 
 
 def compressed_kv_verify(query, view, scale):
     """Multi-query verify over a packed view, or None when unsupported.
 
     query [1, Hq, n, D] holds the last n positions (already appended to the
-    view's residual); rows n * Hq/Hkv must not exceed 16.
+    view's window); the n * Hq/Hkv query rows of a KV head must not exceed 16.
     """
-    if not _query_ok(query, scale) or query.shape[2] < 1 or view.packed_tokens < 128:
-        return None
-    if not _view_ok(query, view, query.shape[2]):
-        return None
-    if query.shape[2] * (query.shape[1] // view.keys.shape[1]) > 16:
-        return None
-    try:
-        from .compressed_kv_kernels import verify
-    except ImportError:
-        return None
-    return verify(query, view, scale)
+    return _run_guarded(query, view, scale, VERIFY_ROUTE)
 
 
 def _supported_mask(mask, length, queries=1):
-    """None, or a lower-right causal bias of ``queries`` x ``length`` (``:32-37``)."""
+    """Masks the kernels reproduce exactly (reference ``:32-37``).
+
+    One query: None or a lower-right causal bias of 1 x ``length``.  Several
+    queries: only the lower-right causal bias of ``queries`` x ``length``.
+    Upstream attention given no mask for several queries aligns its causal
+    mask top-left (SDPA ``is_causal``), which is not the kernels' rule, so
+    that call stays on the upstream path.
+    """
     if mask is None:
-        return True
+        return queries == 1
     from torch.nn.attention.bias import CausalBias, CausalVariant
     return (type(mask) is CausalBias and mask.variant == CausalVariant.LOWER_RIGHT
             and mask.seq_len_q == queries and mask.seq_len_kv == length)
@@ -112,13 +110,13 @@ def _forward(self, hidden_states, position_embeddings, attention_mask, past_key_
     if past_key_values is not None and self.layer_idx < len(past_key_values.layers):
         layer = past_key_values.layers[self.layer_idx]
     q_len = hidden_states.shape[1] if hidden_states.ndim == 3 else 0
-    verify = q_len > 1 and q_len <= 4 and mtp_verification_enabled()
+    verify = q_len > 1 and q_len <= 4 and _scope.mtp_verification_enabled()
     prefill = 16 <= q_len <= getattr(self, '_direct_kv_prefill_max', 0)
     eligible = (self._direct_kv_enabled and not self.training and not torch.is_grad_enabled()
                 and not torch.is_autocast_enabled('cuda') and hidden_states.is_cuda
                 and hidden_states.shape[0] == 1 and (q_len == 1 or verify or prefill)
                 and hidden_states.dtype in (torch.bfloat16, torch.float16)
-                and isinstance(layer, QuantizedAttentionLayer) and layer.key_bank.units > 0
+                and _quantized_layer(layer) and layer.key_bank.units > 0
                 and self.head_dim in (64, 128, 256) and self.config._attn_implementation == 'sdpa'
                 and not kwargs.get('output_attentions', False) and kwargs.get('head_mask') is None
                 and all(value is None or name in ('is_causal', 'output_attentions', 'use_cache', 'position_ids')

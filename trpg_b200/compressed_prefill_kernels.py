@@ -3,7 +3,8 @@
 Mirror of ``models/compressed_prefill_kernels.py:98-111``: ``prefill(query,
 view, scale)`` runs after the public eligibility checks of
 ``trpg_b200.compressed_prefill_attention.compressed_kv_prefill`` and reads
-the whole history once per CTA of 64 query rows (n-major over the G query
+the whole history once per CTA of 128 query rows (``BM`` in
+``csrc/ckv_prefill.cu``: 8 warps of 16 rows, position-major over the G query
 heads of a KV head), never materialising the dequantized history.
 """
 from __future__ import annotations

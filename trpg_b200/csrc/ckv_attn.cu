@@ -916,13 +916,16 @@ template <int BITS, int D, int NT, int DT, int MAXS>
 int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
   using C = Cfg<BITS, D, NT>;
   auto kern = attn_kernel<BITS, D, NT, DT, MAXS>;
-  static std::atomic<int> configured[64];
+  // The shared-memory attribute belongs to the device's context: set once
+  // per context (a cudaDeviceReset gives the device a new one).
+  static std::atomic<unsigned long long> configured[64];
   int dev = 0;
   CKV_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return CKV_ERR_INVALID;
-  if (!configured[dev].load(std::memory_order_acquire)) {
+  const unsigned long long ctx = context_id();
+  if (ctx == 0 || configured[dev].load(std::memory_order_acquire) != ctx) {
     CKV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    configured[dev].store(1, std::memory_order_release);
+    configured[dev].store(context_id(), std::memory_order_release);
   }
   Params<MAXS> &p = params_scratch<MAXS>();
   memset(&p, 0, sizeof(ParamsHead) + sizeof(SeqDev) * a.num_seqs);
@@ -1027,8 +1030,11 @@ extern "C" int ckv_attention(const ckv_attn_args *args, void *workspace, size_t 
   return args->bits == 8 ? dispatch_d<8>(*args, pl, ws, st) : dispatch_d<4>(*args, pl, ws, st);
 }
 
+int static_scratch_error(int *flag, ckv_stream_t stream);   // ckv_static.cu
+
 extern "C" int ckv_attention_error(const void *workspace, int *flag, ckv_stream_t stream) {
-  if (!workspace || !flag) return CKV_ERR_INVALID;
+  if (!flag) return CKV_ERR_INVALID;
+  if (!workspace) return static_scratch_error(flag, stream);
   unsigned v = 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   CKV_CUDA_TRY(cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, st));

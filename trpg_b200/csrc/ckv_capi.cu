@@ -1,4 +1,5 @@
 // Status strings, per-thread error text and version of the C ABI.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <string.h>
@@ -20,6 +21,31 @@ int cuda_status(cudaError_t err) {
   snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(err),
            cudaGetErrorString(err));
   return CKV_ERR_CUDA;
+}
+
+namespace {
+using CtxGetCurrent = CUresult (*)(CUcontext *);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long *);
+
+template <class F>
+F driver_fn(const char *name) {
+  void *ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(ptr);
+}
+}  // namespace
+
+unsigned long long context_id() {
+  static const CtxGetCurrent get_current = driver_fn<CtxGetCurrent>("cuCtxGetCurrent");
+  static const CtxGetId get_id = driver_fn<CtxGetId>("cuCtxGetId");
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
 }
 }  // namespace ckv
 

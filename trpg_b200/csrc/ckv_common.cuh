@@ -15,6 +15,10 @@ namespace ckv {
 // ---------------------------------------------------------------------------
 void set_last_error(const char *msg);
 int cuda_status(cudaError_t err);   // records the string, returns CKV_ERR_CUDA
+// Unique id of the calling thread's current CUDA context, 0 when there is
+// none yet.  Ids are never reused, so state cached per context (a device
+// address, a function attribute) is known stale after a cudaDeviceReset.
+unsigned long long context_id();
 
 #define CKV_CUDA_TRY(expr)                          \
   do {                                              \

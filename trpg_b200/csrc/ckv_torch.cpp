@@ -176,6 +176,18 @@ Tensor fit_rows(const Tensor &t) {
   return ok ? t : fit_copy(t);
 }
 
+// A window view [1,H,r,D] whose rows sit in a buffer of `capacity` rows per
+// head: dense rows of D elements, heads `capacity * D` apart, and a storage
+// large enough for all of them.  Anything else is not a window this op may
+// write past the end of.
+bool window_holds(const Tensor &w, int64_t capacity) {
+  if (w.dim() != 4 || w.size(0) != 1 || w.stride(3) != 1 || w.stride(2) != w.size(3)) return false;
+  const int64_t H = w.size(1), D = w.size(3);
+  if (H > 1 && w.stride(1) != capacity * D) return false;
+  const int64_t need = w.storage_offset() + (H - 1) * capacity * D + capacity * D;
+  return int64_t(w.storage().nbytes()) >= need * int64_t(w.element_size());
+}
+
 // keys[:, :, offset:offset+n] = keys_new (and values) for window buffers
 // [1,H,C,D] with capacity C >= offset + n; one launch.
 // Writes the new rows at `offset` and returns the window views of the rows
@@ -220,6 +232,26 @@ std::tuple<Tensor, Tensor> residual_append(const Tensor &keys_new, const Tensor 
   check_status(ckv_residual_append(&a, current_stream(keys)), "residual_append");
   const int64_t rows = offset + keys_new.size(2);
   return {keys.narrow(2, 0, rows), values.narrow(2, 0, rows)};
+}
+
+// Append to the exact window in place: `keys` / `values` are the current
+// window views [1,H,r,D] of buffers with `capacity` rows per head.  The new
+// rows go to rows [r, r + n) (past the end of the views, so views handed out
+// earlier keep their contents) and the views of the first r + n rows come
+// back.  The buffer geometry is re-derived from the views and checked against
+// their storage before anything is written.
+std::tuple<Tensor, Tensor> window_append(const Tensor &keys_new, const Tensor &values_new,
+                                         const Tensor &keys, const Tensor &values,
+                                         int64_t capacity) {
+  TORCH_CHECK(keys.dim() == 4 && values.sizes() == keys.sizes(),
+              "ckv::window_append: window views must be [1,H,r,D]");
+  TORCH_CHECK(window_holds(keys, capacity) && window_holds(values, capacity),
+              "ckv::window_append: the views are not rows of a window buffer of capacity ", capacity);
+  const int64_t H = keys.size(1), D = keys.size(3), r = keys.size(2);
+  const std::vector<int64_t> full{1, H, capacity, D}, st{H * capacity * D, capacity * D, D, 1};
+  const Tensor kb = keys.as_strided(full, st, keys.storage_offset());
+  const Tensor vb = values.as_strided(full, st, values.storage_offset());
+  return residual_append(keys_new, values_new, kb, vb, r);
 }
 
 // ---------------------------------------------------------------------------
@@ -421,36 +453,89 @@ Tensor decode(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor 
   return out;
 }
 
-// compressed_kv_decode's guard (models/compressed_kv_attention.py:8-29), in
-// one call: nullopt for anything the kernel does not cover (the caller then
-// falls back to SDPA), else decode's output.  The checks match
-// trpg_b200.compressed_kv_attention._query_ok / _view_ok.
-std::optional<Tensor> decode_guarded(const Tensor &q, const std::optional<Tensor> &kd,
-                                     const std::optional<Tensor> &km,
-                                     const std::optional<Tensor> &vd,
-                                     const std::optional<Tensor> &vm,
-                                     const std::optional<Tensor> &rk,
-                                     const std::optional<Tensor> &rv, int64_t packed,
-                                     int64_t length, int64_t bits, double scale) {
-  if (!q.is_cuda() || at::GradMode::is_enabled() || at::autocast::is_autocast_enabled(at::kCUDA))
-    return std::nullopt;
-  if (q.dim() != 4 || q.size(0) != 1 || q.size(2) != 1 || q.requires_grad() || q.stride(3) != 1)
-    return std::nullopt;
+Tensor prefill(const Tensor &q, const Tensor &kd, const Tensor &km, const Tensor &vd,
+               const Tensor &vm, const Tensor &rk, const Tensor &rv, int64_t packed,
+               int64_t length, int64_t bits, double scale);
+
+// Routes of the guarded entry points.
+enum Route : int64_t { kDecode = 0, kVerify = 1, kPrefill = 2 };
+
+using OptTensor = std::optional<Tensor>;
+
+// Whether a kernel of this library covers the call; when it does not, the
+// guarded op returns None and the caller falls back to dequantize + SDPA.
+// The acceptance rules are those of the reference's guards -- one query:
+// models/compressed_kv_attention.py:8-29; a chunk of 16..4096 queries with
+// the bank shapes checked too: models/compressed_prefill_attention.py:6-52 --
+// plus the verify route's limit of 16 query rows per KV head.  They are
+// checked in the order the kernel touches the data: autograd state, the
+// query, the presence of every cache tensor, the exact window, the banks.
+bool covers(Route route, const Tensor &q, const OptTensor *view, int64_t packed, int64_t length,
+            int64_t bits, double scale) {
+  if (!q.is_cuda() || at::GradMode::is_enabled() || at::autocast::is_autocast_enabled(at::kCUDA) ||
+      q.requires_grad())
+    return false;
+  if (q.dim() != 4 || q.size(0) != 1 || q.stride(3) != 1) return false;
   const auto dt = q.scalar_type();
-  const int64_t d = q.size(3);
-  if ((dt != at::kBFloat16 && dt != at::kHalf) || (d != 64 && d != 128 && d != 256) ||
-      !std::isfinite(scale) || (bits != 4 && bits != 8) || packed < 128)
-    return std::nullopt;
-  for (const auto *t : {&kd, &km, &vd, &vm, &rk, &rv})
-    if (!t->has_value() || !(*t)->defined() || (*t)->device() != q.device() || (*t)->requires_grad())
-      return std::nullopt;
-  const Tensor &keys = *rk, &values = *rv;
-  if (keys.dim() != 4 || values.sizes() != keys.sizes() || keys.size(0) != 1 ||
-      keys.scalar_type() != dt || values.scalar_type() != dt || keys.size(3) != d ||
-      q.size(1) % keys.size(1) != 0 || q.size(1) / keys.size(1) > 16 ||
-      length != packed + keys.size(2) || keys.stride(3) != 1 || values.stride(3) != 1)
-    return std::nullopt;
-  return decode(q, *kd, *km, *vd, *vm, keys, values, packed, length, bits, scale);
+  const int64_t n = q.size(2), d = q.size(3), hq = q.size(1);
+  if ((dt != at::kBFloat16 && dt != at::kHalf) || (d != 64 && d != 128 && d != 256)) return false;
+  if (!std::isfinite(scale) || (bits != 4 && bits != 8)) return false;
+  const bool chunk = route == kPrefill;
+  if (chunk ? (n < 16 || n > 4096) : (route == kDecode ? n != 1 : n < 1)) return false;
+  if (packed < (chunk ? 1 : 128) || packed % 128) return false;
+  for (int i = 0; i < 6; ++i) {
+    const OptTensor &t = view[i];
+    if (!t.has_value() || !t->defined() || t->device() != q.device() || t->requires_grad())
+      return false;
+  }
+  // The exact window: [1,H,R,D] in the query dtype, rows dense, and long
+  // enough to hold every query position.
+  const Tensor &keys = *view[4], &values = *view[5];
+  if (keys.dim() != 4 || values.sizes() != keys.sizes() || keys.size(0) != 1) return false;
+  const int64_t h = keys.size(1), r = keys.size(2);
+  if (h < 1 || hq < 1 || hq % h || hq / h > 16 || keys.size(3) != d) return false;
+  if (keys.scalar_type() != dt || values.scalar_type() != dt) return false;
+  if (keys.stride(3) != 1 || values.stride(3) != 1 || length != packed + r) return false;
+  if (route != kDecode && r < n) return false;
+  if (route == kVerify && n * (hq / h) > 16) return false;
+  if (!chunk) return true;
+  // The banks, [1,H,rows,...]: key codes (D, 128*bits/8) and meta (D, 2) per
+  // 128-token unit; value codes (D/64, 64*bits/8) and meta (D/64, 2) per token.
+  const Tensor &kd = *view[0], &km = *view[1], &vd = *view[2], &vm = *view[3];
+  const int64_t per = 8 / bits;
+  struct Want { const Tensor *t; at::ScalarType type; int64_t rows, a, b; };
+  const Want want[4] = {{&kd, at::kByte, packed / 128, d, 128 / per},
+                        {&km, at::kFloat, packed / 128, d, 2},
+                        {&vd, at::kByte, packed, d / 64, 64 / per},
+                        {&vm, at::kFloat, packed, d / 64, 2}};
+  for (const Want &w : want) {
+    const Tensor &t = *w.t;
+    if (t.dim() != 5 || t.scalar_type() != w.type || t.size(0) != 1 || t.size(1) != h ||
+        t.size(2) < w.rows || t.size(3) != w.a || t.size(4) != w.b || t.stride(4) != 1)
+      return false;
+  }
+  return true;
+}
+
+// One call for the guard and the kernel: None when `covers` says no, else
+// the route's output.
+OptTensor attention_guarded(const Tensor &q, const OptTensor &kd, const OptTensor &km,
+                            const OptTensor &vd, const OptTensor &vm, const OptTensor &rk,
+                            const OptTensor &rv, int64_t packed, int64_t length, int64_t bits,
+                            double scale, int64_t route) {
+  const OptTensor view[6] = {kd, km, vd, vm, rk, rv};
+  TORCH_CHECK(route >= kDecode && route <= kPrefill, "ckv::attention_guarded: unknown route ", route);
+  if (!covers(Route(route), q, view, packed, length, bits, scale)) return std::nullopt;
+  if (route == kPrefill) return prefill(q, *kd, *km, *vd, *vm, *rk, *rv, packed, length, bits, scale);
+  return decode(q, *kd, *km, *vd, *vm, *rk, *rv, packed, length, bits, scale);
+}
+
+// The single-query route, the decode loop's entry (one argument fewer).
+OptTensor decode_guarded(const Tensor &q, const OptTensor &kd, const OptTensor &km,
+                         const OptTensor &vd, const OptTensor &vm, const OptTensor &rk,
+                         const OptTensor &rv, int64_t packed, int64_t length, int64_t bits,
+                         double scale) {
+  return attention_guarded(q, kd, km, vd, vm, rk, rv, packed, length, bits, scale, kDecode);
 }
 
 // Packed prefill over one sequence's whole history
@@ -557,8 +642,15 @@ TORCH_LIBRARY(ckv, m) {
       "Tensor? value_meta, Tensor? keys, Tensor? values, int packed, int length, int bits, "
       "float scale) -> Tensor?",
       &decode_guarded);
+  m.def(
+      "attention_guarded(Tensor query, Tensor? key_data, Tensor? key_meta, Tensor? value_data, "
+      "Tensor? value_meta, Tensor? keys, Tensor? values, int packed, int length, int bits, "
+      "float scale, int route) -> Tensor?",
+      &attention_guarded);
   m.def("residual_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
         "int offset) -> (Tensor(a), Tensor(b))");
+  m.def("window_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
+        "int capacity) -> (Tensor(a), Tensor(b))");
 }
 
 namespace {
@@ -595,5 +687,6 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("decode", &decode);
   m.impl("attention_error", &attention_error);
   m.impl("residual_append", &residual_append);
+  m.impl("window_append", &window_append);
   m.impl("prefill", &prefill);
 }

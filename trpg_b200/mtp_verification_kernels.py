@@ -1,14 +1,29 @@
 """Request-local opt-in for multi-query (MTP) verification kernels.
 
-Mirror of ``models/mtp_verification_kernels.py:11-25``: a ContextVar flag
-that nested scopes, exceptions and independent threads/tasks each keep for
-themselves.  ``compressed_kv_attention._forward`` routes 2..4-query calls to
-the compressed-KV verify kernel only inside this scope.
+Same interface as ``models/mtp_verification_kernels.py:11-25``: a flag that
+nested scopes, exceptions and independent threads/tasks each keep for
+themselves, read by ``compressed_kv_attention._forward`` to route 2..4-query
+calls to the verify kernel.
+
+There must be one flag, not two: the reference's MTP loop
+(``models/mtp_generation.py:15,86``) enters the scope of whatever module it
+imported.  ``trpg_b200.install`` therefore maps the reference module name to
+this module, and, when the reference module was imported before that,
+``bind()`` adopts its flag object, so that the scope functions of both
+modules set the flag this package reads.
 """
 from contextlib import contextmanager
 from contextvars import ContextVar
 
 _MTP_VERIFICATION_ENABLED = ContextVar('mtp_verification_kernels_enabled', default=False)
+
+
+def bind(flag: ContextVar) -> None:
+    """Use ``flag`` (the reference module's ContextVar) as this module's flag."""
+    global _MTP_VERIFICATION_ENABLED
+    if not isinstance(flag, ContextVar):
+        raise TypeError('expected the ContextVar of the reference scope module')
+    _MTP_VERIFICATION_ENABLED = flag
 
 
 def mtp_verification_enabled():
@@ -17,8 +32,9 @@ def mtp_verification_enabled():
 
 @contextmanager
 def mtp_verification_scope(enabled=True):
-    token = _MTP_VERIFICATION_ENABLED.set(bool(enabled))
+    flag = _MTP_VERIFICATION_ENABLED
+    token = flag.set(bool(enabled))
     try:
         yield
     finally:
-        _MTP_VERIFICATION_ENABLED.reset(token)
+        flag.reset(token)

@@ -23,8 +23,14 @@ Two steps change:
   launch (``ckv_residual_append``).  ``keys`` / ``values`` are views of its
   first R rows; earlier views are never written again (appends go past
   their end, and compaction moves the rest to a new buffer), so snapshots
-  taken by ``HybridCacheTransaction`` stay valid.  A rolled-back view that
-  is appended to again takes the place of the discarded tokens.
+  taken by ``HybridCacheTransaction`` stay valid.  The layer keeps only
+  plain integers about the buffer (its address, capacity and the rows
+  written so far), so the transaction's snapshot of ``vars(layer)`` --
+  tensors only under ``keys`` / ``values`` -- captures the whole state:
+  after a rollback the restored integers and views agree, and the next
+  append takes the place of the discarded tokens.  A view that is not the
+  end of the rows this layer wrote (a snapshot restored by other means, a
+  tensor set from outside) is copied to a new buffer before any append.
 
 CUDA tensors only: the quantizer and dequantizer have no CPU path here.
 """
@@ -44,21 +50,17 @@ WINDOW_MIN = 512          # tokens of exact-window capacity (compaction keeps it
 VALUE_SLAB_TOKENS = 4096  # models/quantized_kv.py:51
 
 
-_residual_append_op = None
+_window_op = None
 
 
-def _residual_op():
-    global _residual_append_op
-    if _residual_append_op is None:
-        _residual_append_op = ops().residual_append
-    return _residual_append_op
-
-
-def _residual_append(keys_new, values_new, kb, vb, offset):
-    """One launch writes the new key and value rows into the window buffers
-    (the op copies rows it cannot read directly); returns the window views of
-    the first offset + n rows."""
-    return _residual_op()(keys_new, values_new, kb, vb, offset)
+def _window_append(keys_new, values_new, keys, values, capacity):
+    """One launch writes the new key and value rows after the window views
+    ``keys`` / ``values`` (buffers of ``capacity`` rows per head) and returns
+    the views of the rows written so far."""
+    global _window_op
+    if _window_op is None:
+        _window_op = ops().window_append
+    return _window_op(keys_new, values_new, keys, values, capacity)
 
 
 def _pack(rows, bits, rounding=None):
@@ -156,26 +158,29 @@ class QuantizedAttentionLayer(DynamicLayer):
         self.bits = bits
         self.rounding = rounding or _kernels.DEFAULT_ROUNDING
         self.cumulative_length = 0
-        self._window = None   # (key buffer, value buffer, keys view, values view, rows, capacity)
+        # The exact window's buffers: key / value base addresses, rows per
+        # head, and rows written by this layer (0: no buffer).
+        self._window_kptr = self._window_vptr = 0
+        self._window_cap = self._window_rows = 0
         self.key_bank = _PackedBank(bits, 'key', self.rounding)
         self.value_bank = _PackedBank(bits, 'value', self.rounding)
 
     def append_for_attention(self, key_states, value_states):
         """``models/quantized_kv.py:103-114``, appending in place to the window buffer."""
         n = key_states.shape[-2]
-        w = self._window
-        if w is not None and self.keys is w[2] and self.values is w[3] and w[4] + n <= w[5]:
-            # Fast path: keys / values are the views this layer made last time
-            # (the op checks dtype and device).
-            r = w[4]
-            keys, values = (_residual_append_op or _residual_op())(key_states, value_states,
-                                                                   w[0], w[1], r)
-            self.keys, self.values = keys, values
-            self._window = (w[0], w[1], keys, values, r + n, w[5])
-            self.cumulative_length += n
-            kb, vb = self.key_bank, self.value_bank
-            return QuantizedKVView(kb.data, kb.meta, vb.data, vb.meta, kb.units * 128, keys, values,
-                                   self.bits, self.cumulative_length)
+        cap, rows = self._window_cap, self._window_rows
+        if cap and rows + n <= cap:
+            keys, values = self.keys, self.values
+            if (keys.shape[2] == rows and keys.data_ptr() == self._window_kptr
+                    and values.data_ptr() == self._window_vptr):
+                # Fast path: the views end at the rows this layer wrote (the op
+                # checks dtype, device and the buffer geometry).
+                self.keys, self.values = _window_append(key_states, value_states, keys, values, cap)
+                self._window_rows = rows + n
+                self.cumulative_length += n
+                kb, vb = self.key_bank, self.value_bank
+                return QuantizedKVView(kb.data, kb.meta, vb.data, vb.meta, kb.units * 128,
+                                       self.keys, self.values, self.bits, self.cumulative_length)
         if key_states.shape[-1] % 64 or value_states.shape[-1] % 64:
             raise ValueError('quantized KV needs head_dim to be a multiple of 64')
         if not self.is_initialized:
@@ -183,51 +188,44 @@ class QuantizedAttentionLayer(DynamicLayer):
         self.cumulative_length += n
         if not (key_states.is_cuda and key_states.dim() == 4 and key_states.shape[0] == 1
                 and key_states.dtype in (torch.bfloat16, torch.float16)
-                and value_states.shape == key_states.shape and value_states.dtype == key_states.dtype):
+                and value_states.shape == key_states.shape and value_states.dtype == key_states.dtype
+                and (self.keys.dim() != 4 or (self.keys.dtype == key_states.dtype
+                                              and self.keys.shape[1] == key_states.shape[1]
+                                              and self.keys.shape[3] == key_states.shape[3]))):
             self.keys = torch.cat((self.keys, key_states), dim=-2)
             self.values = torch.cat((self.values, value_states), dim=-2)
-            self._window = None
+            self._forget_window()
         else:
-            kb, vb = self._window_for(key_states, n)
             r = self.keys.shape[-2] if self.keys.dim() == 4 else 0
-            self.keys, self.values = _residual_append(key_states, value_states, kb, vb, r)
-            self._window = (kb, vb, self.keys, self.values, r + n, kb.shape[2])
+            self._new_window(key_states, r + n, self.keys if r else None, self.values if r else None)
+            self.keys, self.values = _window_append(key_states, value_states, self.keys, self.values,
+                                                    self._window_cap)
+            self._window_rows = r + n
         return QuantizedKVView(self.key_bank.data, self.key_bank.meta,
                                self.value_bank.data, self.value_bank.meta,
                                self.key_bank.units * 128, self.keys, self.values,
                                self.bits, self.cumulative_length)
 
-    def _set_window(self, kb, vb, r):
-        """keys / values = the first r rows of the window buffers."""
-        self.keys, self.values = kb.narrow(2, 0, r), vb.narrow(2, 0, r)
-        self._window = (kb, vb, self.keys, self.values, r, kb.shape[2])
-
-    def _window_for(self, like, n):
-        """Window buffers that hold ``keys`` / ``values`` as their first rows and
-        have room for ``n`` more; a new pair (with the current rows copied) when
-        the current window is full or ``keys`` is not a prefix of it."""
-        window = self._window
-        r = self.keys.shape[-2] if self.keys.dim() == 4 else 0
-        if window is not None:
-            kb, vb = window[0], window[1]
-            if (self.keys.dim() == 4 and self.keys.data_ptr() == kb.data_ptr()
-                    and self.values.data_ptr() == vb.data_ptr() and self.keys.stride() == kb.stride()
-                    and self.values.stride() == vb.stride() and r + n <= kb.shape[2]
-                    and kb.dtype == like.dtype and kb.device == like.device
-                    and kb.shape[1] == like.shape[1] and kb.shape[3] == like.shape[3]):
-                return kb, vb
-        return self._new_window(like, r + n, self.keys if r else None, self.values if r else None)
+    def _forget_window(self):
+        self._window_kptr = self._window_vptr = 0
+        self._window_cap = self._window_rows = 0
 
     def _new_window(self, like, need, keys=None, values=None):
+        """Fresh window buffers with room for ``need`` rows plus 256 more; the
+        rows of ``keys`` / ``values`` (if given) are copied to their start and
+        ``self.keys`` / ``self.values`` become the views of those rows."""
         b, h, _, d = like.shape
-        cap = max(WINDOW_MIN, -(-need // 128) * 128 + 256)   # room for 256 more tokens
+        cap = max(WINDOW_MIN, -(-need // 128) * 128 + 256)
         kb = torch.empty((b, h, cap, d), dtype=like.dtype, device=like.device)
         vb = torch.empty_like(kb)
+        r = 0
         if keys is not None:
-            kb[:, :, :keys.shape[2]].copy_(keys)
-            vb[:, :, :values.shape[2]].copy_(values)
-        self._window = (kb, vb, None, None, 0, cap)
-        return kb, vb
+            r = keys.shape[2]
+            kb[:, :, :r].copy_(keys)
+            vb[:, :, :r].copy_(values)
+        self.keys, self.values = kb.narrow(2, 0, r), vb.narrow(2, 0, r)
+        self._window_kptr, self._window_vptr = kb.data_ptr(), vb.data_ptr()
+        self._window_cap, self._window_rows = cap, r
 
     def compact_residual(self):
         """``models/quantized_kv.py:116-124``, quantizing straight into the slabs."""
@@ -247,9 +245,7 @@ class QuantizedAttentionLayer(DynamicLayer):
         self.value_bank.units = units + count // 128
         # The rest moves to a new window (the reference clones it); the old
         # buffer, and every view of it handed out, stays as it was.
-        kb, vb = self._new_window(self.keys, r - count, self.keys[..., count:, :],
-                                  self.values[..., count:, :])
-        self._set_window(kb, vb, r - count)
+        self._new_window(self.keys, r - count, self.keys[..., count:, :], self.values[..., count:, :])
 
     def update(self, key_states, value_states, *args, **kwargs):
         """``models/quantized_kv.py:126-134``: dequantized history + residual."""
