@@ -439,9 +439,16 @@ def b200_arm(args, world, rank, local):
     seq.rollback()
 
     # ---- roofline of the decode kernel (the clock window extends over it) ----
+    from trpg_b200.compressed_kv_kernels import dequant, set_dequant
+    rule = dequant()
     sec, bytes_per_launch, replays = time_kernel(seq, decode)
     clocks.stop()
     sec = max_over_ranks(sec, world)
+    # The same launches under the other dequantization rule, for comparison.
+    other = 'exact' if rule == 'folded' else 'folded'
+    set_dequant(other)
+    sec_other = max_over_ranks(time_kernel(seq, decode, min_seconds=0.2)[0], world)
+    set_dequant(rule)
     peak, peak_kind = peaks()
     achieved = bytes_per_launch / sec / 1e9
     traffic = None
@@ -471,7 +478,9 @@ def b200_arm(args, world, rank, local):
                          'frac': achieved / peak, 'traffic': traffic, 'peak_source': peak_kind,
                          'kernel': 'attn_kernel<8,256,1,bf16>',
                          'bytes_per_launch': bytes_per_launch, 'us_per_launch': sec * 1e6,
-                         'launches_timed': replays * LAYERS},
+                         'launches_timed': replays * LAYERS, 'dequant': rule,
+                         'other_rule': {'dequant': other, 'us_per_launch': sec_other * 1e6,
+                                        'frac': bytes_per_launch / sec_other / 1e9 / peak}},
             'hbm_gbs_step': LAYERS * bytes_per_launch / (ms * 1e-3) / 1e9,
             'clocks': clocks.summary(),
             'e2e': {'value': world / (e2e_ms * 1e-3), 'unit': 'tok/s',
@@ -782,6 +791,9 @@ def main():
     ap.add_argument('--steps', type=int, default=1024)
     ap.add_argument('--warmup', type=int, default=16)
     ap.add_argument('--impl', choices=('b200', 'reference'), default='b200')
+    ap.add_argument('--dequant', choices=('exact', 'folded'), default=None,
+                    help='dequantization rule of the attention kernel (default: the library '
+                         'default, TRPG_CKV_DEQUANT or exact)')
     ap.add_argument('--cpu-steps', type=int, default=24)
     ap.add_argument('--cpu-one-thread-steps', type=int, default=3)
     ap.add_argument('--no-cpu', action='store_true')
@@ -795,6 +807,9 @@ def main():
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
     world, rank, local = init_dist()
+    if args.dequant and args.impl == 'b200':
+        from trpg_b200.compressed_kv_kernels import set_dequant
+        set_dequant(args.dequant)
     try:
         if args.impl == 'reference':
             reference_arm(args, world, rank)

@@ -168,6 +168,14 @@ typedef struct {
 #define CKV_WS_COUNTERS_ZERO 1  /* caller guarantees the workspace header and
                                    ticket region are zero; the call leaves the
                                    tickets at zero */
+#define CKV_DEQUANT_FOLDED 2    /* folded dequantization (head_dim 128 or 256;
+                                   other sizes use the exact rule): the scales
+                                   go into the query and probability operands
+                                   and the codes reach the tensor cores as
+                                   exact fp16 values; results agree with the
+                                   exact rule to fp16 rounding of q*scale and
+                                   p*scale instead of bf16 rounding of every
+                                   dequantized value */
 
 /* Maximum sequences in one ckv_attention call (the per-sequence descriptors,
  * TMA tensor maps included, travel as kernel parameters). */

@@ -42,7 +42,7 @@ def check(actual, expected):
 
 @pytest.mark.parametrize('case', sorted({k[:-5] for k in np.load(GOLDEN / 'attention.npz').files
                                          if k.endswith('_spec')}))
-def test_matches_reference_outputs_and_oracle(case):
+def test_matches_reference_outputs_and_oracle(case, both_rules):
     a = np.load(GOLDEN / 'attention.npz')
     bits, hkv, hq, length, dim, n, seed, outliers = (int(x) for x in a[f'{case}_spec'])
     dtype, scale = str(a[f'{case}_dtype']), float(a[f'{case}_scale'])
@@ -56,7 +56,7 @@ def test_matches_reference_outputs_and_oracle(case):
 
 @pytest.mark.parametrize('bits', [8, 4])
 @pytest.mark.parametrize('residual', [1, 16, 64, 128, 129, 255, 256, 300])
-def test_residual_window_sweep(bits, residual):
+def test_residual_window_sweep(bits, residual, both_rules):
     """Hand-built views: any residual length next to 3 packed blocks."""
     from trpg_b200.quantized_kv import QuantizedAttentionLayer, QuantizedKVView
     k = O.seeded_normal(5, (1, 4, 384 + residual, 256))
@@ -79,19 +79,19 @@ def test_residual_window_sweep(bits, residual):
 
 @pytest.mark.parametrize('nq', [2, 3, 4])
 @pytest.mark.parametrize('bits', [8, 4])
-def test_verify_lower_right_causal(nq, bits):
+def test_verify_lower_right_causal(nq, bits, both_rules):
     layer, view, ol = gpu_cache_state(40 + nq, 4, 1000 + 77 * nq, 256, bits, nq)
     q = O.seeded_normal(50 + nq, (1, 16, nq, 256))
     check(run(to_torch(q, 'bfloat16'), view, 1 / 16), O.decode_reference(q, ol, 1 / 16))
 
 
-def test_verify_sixteen_rows_with_fp16_and_d128():
+def test_verify_sixteen_rows_with_fp16_and_d128(both_rules):
     layer, view, ol = gpu_cache_state(61, 2, 2222, 128, 8, 2, 'float16')
     q = O.seeded_normal(62, (1, 16, 2, 128), 'float16')      # 8 groups x 2 queries = 16 rows
     check(run(to_torch(q, 'float16'), view, 128 ** -.5), O.decode_reference(q, ol, 128 ** -.5))
 
 
-def test_large_logits_stay_finite_and_unsupported_inputs_return_none():
+def test_large_logits_stay_finite_and_unsupported_inputs_return_none(both_rules):
     layer, view, ol = gpu_cache_state(71, 2, 512, 64, 4)
     keys = view.keys
     q = keys[..., :1, :].repeat_interleave(2, dim=1) * 80
@@ -144,7 +144,7 @@ def test_fused_dequant_rounding_known_answer(bank):
     torch.testing.assert_close(actual[..., :1], expected[..., :1], rtol=0, atol=.002)
 
 
-def test_batched_ragged_call_equals_per_sequence_calls():
+def test_batched_ragged_call_equals_per_sequence_calls(both_rules):
     from trpg_b200.compressed_kv_kernels import attention
     qs, views, want = [], [], []
     for i, length in enumerate((700, 1900, 2600, 3333, 5000)):
@@ -160,7 +160,7 @@ def test_batched_ragged_call_equals_per_sequence_calls():
 
 
 @pytest.mark.parametrize('world', [2, 3, 8])
-def test_split_kv_partials_combine_to_the_full_result(world):
+def test_split_kv_partials_combine_to_the_full_result(world, both_rules):
     from trpg_b200 import sharding
     from trpg_b200.compressed_kv_kernels import attention, combine
     layer, view, ol = gpu_cache_state(81, 4, 9000, 256, 4)
@@ -253,3 +253,53 @@ def test_window_appends_in_place_and_keeps_earlier_views():
         again = layer.append_for_attention(z, z)
         assert torch.equal(again.keys[..., :-1, :], first[..., :-1, :])
         assert torch.equal(again.keys[..., -1:, :], z)
+
+
+@pytest.mark.parametrize('bits', [8, 4])
+def test_folded_rule_follows_value_and_key_ranges_across_blocks(bits):
+    """Blocks whose value and key magnitudes differ by up to 10^6 from one
+    another (and a block of exact zeros): the folded rule's range exponent
+    moves with them.  The folded rule never rounds a dequantized value, so
+    the reference here is dequantize + SDPA without that rounding (at |v| ~
+    3000 the bf16 rounding of the other rule alone moves outputs by ~1)."""
+    from trpg_b200 import compressed_kv_kernels as K
+    from trpg_b200.quantized_kv import QuantizedAttentionLayer, QuantizedKVView
+    blocks, resid = 24, 200
+    k = O.seeded_normal(81, (1, 4, 128 * blocks + resid, 256))
+    v = O.seeded_normal(82, (1, 4, 128 * blocks + resid, 256))
+    for b in range(blocks):
+        sl = slice(128 * b, 128 * (b + 1))
+        v[:, :, sl] = O.round_to(v[:, :, sl] * np.float32(10.0 ** ((b % 7) - 3)), 'bfloat16')
+        k[:, :, sl] = O.round_to(k[:, :, sl] * np.float32(2.0 ** ((b % 5) - 2)), 'bfloat16')
+    v[:, :, 128 * 5:128 * 6] = 0
+    layer = QuantizedAttentionLayer(bits)
+    with torch.inference_mode():
+        layer.key_bank.reserve(blocks, to_torch(k[:, :, :1], 'bfloat16'), 1, 4, 256)
+        layer.value_bank.reserve(blocks, to_torch(k[:, :, :1], 'bfloat16'), 1, 4, 256)
+        layer.key_bank.append(to_torch(k[:, :, :128 * blocks], 'bfloat16'))
+        layer.value_bank.append(to_torch(v[:, :, :128 * blocks], 'bfloat16'))
+    keys = to_torch(k[:, :, 128 * blocks:], 'bfloat16')
+    values = to_torch(v[:, :, 128 * blocks:], 'bfloat16')
+    view = QuantizedKVView(layer.key_bank.data, layer.key_bank.meta, layer.value_bank.data,
+                           layer.value_bank.meta, 128 * blocks, keys, values, bits,
+                           128 * blocks + resid)
+    ol = O.OracleLayer(bits, dtype='float32')    # dequantized values not rounded to bf16
+    ol._append_bank(k[:, :, :128 * blocks], v[:, :, :128 * blocks])
+    ol.keys, ol.values, ol.length = k[:, :, 128 * blocks:], v[:, :, 128 * blocks:], 128 * blocks + resid
+    q = O.seeded_normal(83, (1, 16, 1, 256))
+    expected = O.decode_reference(q, ol, 1 / 16)
+    err = {}
+    old = K.dequant()
+    try:
+        for rule in ('exact', 'folded'):
+            K.set_dequant(rule)
+            out = run(to_torch(q, 'bfloat16'), view, 1 / 16).float().cpu().numpy()
+            assert np.isfinite(out).all()
+            err[rule] = max_abs(out, expected)
+    finally:
+        K.set_dequant(old)
+    # Outputs average values of magnitude up to ~4000 with heavy cancellation;
+    # a 16-bit rounding anywhere moves them by ~1e-4 of that magnitude.
+    vmax = float(np.abs(v).max())
+    assert err['folded'] <= 1e-3 * vmax, (err, vmax)
+    assert err['folded'] <= 1.5 * err['exact'] + 1e-3, err

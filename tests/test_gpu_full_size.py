@@ -47,7 +47,7 @@ def query(seed, nq=1, dtype='bfloat16'):
     return qn, to_torch(qn, dtype)
 
 
-def test_single_sequence_32k_q8_outliers_across_compaction():
+def test_single_sequence_32k_q8_outliers_across_compaction(both_rules):
     """32768 tokens (32512 packed + 256 window) with 1% of channels x8, then
     160 decode steps on the same layer (a compaction at the 256th window
     token), checked against the oracle at the first step, just before and
@@ -74,7 +74,7 @@ def test_single_sequence_32k_q8_outliers_across_compaction():
     assert layer.key_bank.units == ol.units == units0 + 1
 
 
-def test_two_32k_layers_back_to_back():
+def test_two_32k_layers_back_to_back(both_rules):
     """Two distinct 32K caches decoded one after the other on one stream (the
     benchmark's layer loop), each checked."""
     from trpg_b200.compressed_kv_kernels import decode
@@ -86,7 +86,7 @@ def test_two_32k_layers_back_to_back():
         check(out, O.decode_reference_chunked(qn, ol, SCALE))
 
 
-def test_batch_of_64_ragged_sequences_in_one_launch():
+def test_batch_of_64_ragged_sequences_in_one_launch(both_rules):
     """64 sequences, contexts uniform in [1024, 8192], one query each, Q8:
     one kernel launch over all (sequence, KV head) pairs."""
     from trpg_b200.compressed_kv_kernels import MAX_SEQS, attention
@@ -101,7 +101,7 @@ def test_batch_of_64_ragged_sequences_in_one_launch():
         check(out, O.decode_reference_chunked(qn, ol, SCALE))
 
 
-def test_verify_16_sequences_4_queries_16k():
+def test_verify_16_sequences_4_queries_16k(both_rules):
     """16 sequences x 4 query positions (lower-right causal among them) over
     16384 tokens, Q8: 16 query rows per KV head, the two-tile variant."""
     from trpg_b200.compressed_kv_kernels import attention
@@ -121,7 +121,7 @@ def long_q4():
     return layer, view, ol, qn, qt, expected
 
 
-def test_long_context_q4_131k_whole(long_q4):
+def test_long_context_q4_131k_whole(long_q4, both_rules):
     from trpg_b200.compressed_kv_kernels import decode
     layer, view, ol, qn, qt, expected = long_q4
     assert view.packed_tokens == 130816 and view.keys.shape[2] == 256
@@ -130,7 +130,7 @@ def test_long_context_q4_131k_whole(long_q4):
 
 
 @pytest.mark.parametrize('world', [2, 4, 8])
-def test_long_context_q4_131k_split_kv_shards(long_q4, world):
+def test_long_context_q4_131k_split_kv_shards(long_q4, world, both_rules):
     """The split-KV partitioning of the multi-GPU path, emulated on one GPU:
     each shard's (o, m, l) partial from its own launch, merged by the
     combine kernel."""

@@ -69,12 +69,17 @@ def _seq(query, view, out):
     return s, (kd, km, vd, vm, rk, rv)     # keep any copies alive for the call
 
 
+CKV_DEQUANT_FOLDED = 2
+
+
 def _args(queries, views, outs, scale):
+    from trpg_b200 import compressed_kv_kernels as K
     seqs, keep = zip(*(_seq(q, v, o) for q, v, o in zip(queries, views, outs)))
     arr = (Seq * len(seqs))(*seqs)
     q = queries[0]
+    flags = CKV_DEQUANT_FOLDED if K.dequant() == 'folded' else 0   # the rule the torch ops use
     args = AttnArgs(arr, len(seqs), q.shape[1], views[0].keys.shape[1], q.shape[3], q.shape[2],
-                    views[0].bits, DTYPE[q.dtype], scale, 0, 0)
+                    views[0].bits, DTYPE[q.dtype], scale, 0, flags)
     return args, (arr, keep)
 
 
@@ -103,7 +108,7 @@ def test_static_entry_rejects_null_args():
 @pytest.mark.gpu
 @pytest.mark.parametrize('bits,nq,lengths', [(8, 1, [32767]), (8, 1, [1500, 4097, 9000]),
                                              (4, 2, [3000, 700]), (8, 4, [5000])])
-def test_static_matches_workspace_entry_twice(bits, nq, lengths):
+def test_static_matches_workspace_entry_twice(bits, nq, lengths, both_rules):
     from trpg_b200 import compressed_kv_kernels as K
     queries, views = _batch(11 * bits + nq, lengths, bits, nq)
     scale = 256 ** -.5

@@ -8,6 +8,7 @@ missing, every op raises.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import torch
@@ -23,9 +24,11 @@ EXPORTS = ('ckv_status_string', 'ckv_last_error', 'ckv_version', 'ckv_pack_rows'
            'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill')
 
 ROUNDING = {'half_even': 0, 'half_up': 1}
+DEQUANT_MODES = ('exact', 'folded')
 
 _lib = None
 _loaded = False
+_dequant = 'exact'
 
 
 def library() -> ctypes.CDLL:
@@ -50,6 +53,24 @@ def load() -> None:
         raise ImportError(f'{TORCH_LIB_PATH.name} is not built; run `python -m trpg_b200.build`')
     torch.ops.load_library(str(TORCH_LIB_PATH))
     _loaded = True
+    set_dequant(os.environ.get('TRPG_CKV_DEQUANT', 'exact'))
+
+
+def set_dequant(mode: str) -> str:
+    """Dequantization rule of the attention ops ('exact' or 'folded'); returns
+    the previous one.  See ``compressed_kv_kernels.set_dequant``."""
+    global _dequant
+    if mode not in DEQUANT_MODES:
+        raise ValueError(f'dequantization rule must be one of {DEQUANT_MODES}, not {mode!r}')
+    load()
+    torch.ops.ckv.set_dequant(DEQUANT_MODES.index(mode))
+    old, _dequant = _dequant, mode
+    return old
+
+
+def dequant() -> str:
+    load()
+    return _dequant
 
 
 def ops():

@@ -25,9 +25,41 @@ from typing import Sequence
 
 import torch
 
+from . import _native
 from ._native import ops
 
 MAX_SEQS = 64   # CKV_MAX_SEQS in include/ckv.h
+
+DEQUANT_MODES = _native.DEQUANT_MODES
+
+
+def set_dequant(mode: str) -> str:
+    """Select the dequantization rule of every attention call in this process
+    (decode, verify, batched, split-KV); returns the previous one.
+
+    * ``'exact'`` -- each code becomes ``round_to_query_dtype(fma(code,
+      scale, low))`` before it meets the query or the probabilities, the
+      rounding of the reference's own kernel
+      (``models/compressed_kv_kernels.py:47,68``, pinned by the reference's
+      fused-multiply-add known-answer test).
+    * ``'folded'`` -- the scales are multiplied into the query and the
+      probabilities instead (``sum_d (q_d scale_d) code_d + sum_d q_d low_d``,
+      and per token for the values), and the codes reach the tensor cores as
+      exact fp16 values.  Several times fewer instructions per code; the
+      results differ from the exact rule by fp16 rounding of q*scale and
+      p*scale (finer than the bf16 rounding of each dequantized value) and
+      meet the same tolerances against dequantize + SDPA.  Head dims 128 and
+      256; 64 uses the exact rule.
+
+    The environment variable ``TRPG_CKV_DEQUANT`` sets the rule when the
+    library loads (default ``'exact'``).
+    """
+    return _native.set_dequant(mode)
+
+
+def dequant() -> str:
+    """The dequantization rule in force (see ``set_dequant``)."""
+    return _native.dequant()
 
 
 def _inner_dense(t: torch.Tensor) -> torch.Tensor:

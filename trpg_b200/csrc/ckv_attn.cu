@@ -50,9 +50,15 @@ __device__ __forceinline__ bool wait_stage(uint32_t bar, volatile int *slot, int
   return wait_or_abort(bar, ph & 1, abort);
 }
 
-template <int BITS, int D, int NT, int DT, int MAXS>
+// 2^d for an integer-valued d <= 127 (either sign); 0 below the normal range
+// and for -inf or NaN.
+__device__ __forceinline__ float pow2s(float d) {
+  return !(d >= -126.f) ? 0.f : __int_as_float((int(fminf(d, 127.f)) + 127) << 23);
+}
+
+template <int BITS, int D, int NT, int DT, int MAXS, bool FOLD>
 __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant__ Params<MAXS> p) {
-  using C = Cfg<BITS, D, NT>;
+  using C = Cfg<BITS, D, NT, FOLD>;
   using T = typename Elem<DT>::T;
   constexpr int NV = C::NV;
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -119,6 +125,8 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   // wait on the previous kernel), then its exact-window chunks (loaded only
   // after that wait, so they get the whole pipeline to arrive), then the
   // other packed blocks.  item(i) is the range's item at local position i.
+  // (Filling the whole ring before the wait did not help this kernel: its
+  // items are bound by arithmetic, not by the loads.)
   const int npk = max(0, min(n, np - ib));       // packed blocks in the range
   const int nrs = n - npk;                       // window chunks in the range
   auto item = [&](int i) {
@@ -164,19 +172,29 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   pdl_wait();
 
   // Query B fragments (channel order of the MMA k index), filled by the QK
-  // warps while the producers start streaming.
+  // warps while the producers start streaming: 16-bit pairs, or, for the
+  // folded rule, the four channels' values in fp32.
   if (warp < QK_WARPS) {
-    const uint16_t *qb = static_cast<const uint16_t *>(sd.q);
+    const T *qb = static_cast<const T *>(sd.q);
     for (int x = tid; x < C::KQS * NT * 32; x += QK_WARPS * 32) {
       const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
       const int row = 8 * nt + (ln >> 2), cb = 16 * s + 2 * (ln & 3);
-      uint2 v = make_uint2(0, 0);
-      if (row < rows) {
-        const uint16_t *qrow = qb + (head * G + row % G) * sd.q_h + (row / G) * sd.q_n;
-        v.x = qrow[cb] | (uint32_t(qrow[cb + 1]) << 16);
-        v.y = qrow[cb + 8] | (uint32_t(qrow[cb + 9]) << 16);
+      const T *qrow = qb + (head * G + row % G) * sd.q_h + (row / G) * sd.q_n;
+      if constexpr (FOLD) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < rows)
+          v = make_float4(Elem<DT>::to_f32(qrow[cb]), Elem<DT>::to_f32(qrow[cb + 1]),
+                          Elem<DT>::to_f32(qrow[cb + 8]), Elem<DT>::to_f32(qrow[cb + 9]));
+        *reinterpret_cast<float4 *>(smem + C::OFF_Q + x * 16) = v;
+      } else {
+        uint2 v = make_uint2(0, 0);
+        if (row < rows) {
+          const uint16_t *qr = reinterpret_cast<const uint16_t *>(qrow);
+          v.x = qr[cb] | (uint32_t(qr[cb + 1]) << 16);
+          v.y = qr[cb + 8] | (uint32_t(qr[cb + 9]) << 16);
+        }
+        *reinterpret_cast<uint2 *>(smem + C::OFF_Q + x * 8) = v;
       }
-      *reinterpret_cast<uint2 *>(smem + C::OFF_Q + x * 8) = v;
     }
     named_sync(BAR_QFRAG, QK_WARPS * 32);
   }
@@ -190,6 +208,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   const int team = warp < QK_WARPS ? warp / TEAM_WARPS : (warp - QK_WARPS) / TEAM_WARPS;
   float m_run[NT][2], l_run[NT][2];
   float O[C::MTV][NT][4];
+  float Oc[NT][4];     // folded rule: the 1024-offset sum of the value MMAs
+  float2 Ls[NT];       // folded rule: sum of p f low for row 8nt + r (this lane's tokens)
+  int Ex = 0;          // folded rule: this PV warp's range exponent
 
   if (warp >= PRODUCER) {
     // ---- producers: warp PRODUCER streams K stages, PRODUCER + 1 V stages -------
@@ -250,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     __syncwarp();
   } else if (warp < QK_WARPS) {
     // ---- QK warps: team `team`, token quarter q ------------------------------------
-    QkWarp<BITS, D, NT, DT> qw;
+    QkWarp<BITS, D, NT, DT, FOLD> qw;
     qw.lane = lane; qw.r = r; qw.qd = qd; qw.q = warp % TEAM_WARPS;
     qw.qfr = smem + C::OFF_Q;
 #pragma unroll
@@ -270,8 +291,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       const bool have = !s_abort && wait_stage(bar(KFULL + st), &s_issued[st], i, i / NK, &s_abort);
       if (!have && !s_abort) fail();
       if (have) {
-        if (pk) qw.packed(smem + C::OFF_K + st * C::KST, S);
-        else qw.resid(sbase + C::OFF_K + st * C::KST, S[0]);
+        if (pk) {
+          if constexpr (FOLD) qw.packed_fold(sbase + C::OFF_K + st * C::KST, smem + C::OFF_K + st * C::KST, S);
+          else qw.packed(smem + C::OFF_K + st * C::KST, S);
+        } else {
+          qw.resid(sbase + C::OFF_K + st * C::KST, S[0]);
+        }
       } else {
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
@@ -333,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
               if (!pk && mt == 1) continue;
               const float pv = ex2(S[mt][nt][2 * u + j] - muse[nt][j]);
               sum += pv;
-              const int t = pk ? 32 * qw.q + 4 * r + 2 * mt + u : 16 * qw.q + r + 8 * u;
+              const int t = pk ? qw.packed_token(mt, u) : 16 * qw.q + r + 8 * u;
               *reinterpret_cast<T *>(pb + row * PP + ppos(t) * 2) = Elem<DT>::from_f32(pv);
             }
           l_run[nt][j] += sum;
@@ -343,7 +368,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
     }
   } else {
     // ---- PV warps: team `team`, channel quarter c ----------------------------------
-    PvWarp<BITS, D, NT, DT> pw;
+    PvWarp<BITS, D, NT, DT, FOLD> pw;
     pw.lane = lane; pw.r = r; pw.qd = qd; pw.c = (warp - QK_WARPS) % TEAM_WARPS;
 #pragma unroll
     for (int i = 0; i < C::MTV; ++i)
@@ -351,6 +376,12 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int c = 0; c < 4; ++c) O[i][nt][c] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) Oc[nt][c] = 0.f;
+      Ls[nt] = make_float2(0.f, 0.f);
+    }
     // Common scale of this team's accumulator: rows 8nt + 2qd + j (the
     // accumulator columns) and rows 8nt + r (the P fragment columns).
     float Mc[NT][2], Mb[NT];
@@ -367,8 +398,25 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
       if (!ok && !s_abort) fail();
       if (ok) {
         const float *ms = reinterpret_cast<const float *>(smem + C::OFF_XM) + (team * 2 + par) * TEAM_WARPS * C::ROWS;
+        const uint8_t *vst = smem + C::OFF_V + sv * C::VST;
+        // Folded rule: the range exponent of this warp's group, so that the
+        // block's largest scale times 2^Ex is 2^12 (P'' <= 2^12 < fp16 max).
+        // It moves down whenever a block needs it and up only by more than 8
+        // (precision); the accumulators are rescaled by the exact power of two.
+        int dE = 0;
+        if constexpr (FOLD) {
+          if (pk) {
+            const float smax = pw.fold_scale_max(vst);
+            const int eb = ((__float_as_int(smax) >> 23) & 0xff) - 127 + ((__float_as_int(smax) & 0x7fffff) != 0);
+            const int need = smax > 0.f ? max(-60, min(60, 12 - eb)) : Ex;
+            if (need < Ex || need > Ex + 8) {
+              dE = need - Ex;
+              Ex = need;
+            }
+          }
+        }
         // Accumulator rescale: new common scale per accumulator column.
-        bool unit = true;
+        bool unit = dE == 0;
         float2 a2[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -379,7 +427,10 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
             mx0 = fmaxf(mx0, v.x);
             mx1 = fmaxf(mx1, v.y);
           }
-          a2[nt] = make_float2(pow2i(Mc[nt][0] - mx0), pow2i(Mc[nt][1] - mx1));
+          if constexpr (FOLD)
+            a2[nt] = make_float2(pow2s(Mc[nt][0] - mx0 + dE), pow2s(Mc[nt][1] - mx1 + dE));
+          else
+            a2[nt] = make_float2(pow2i(Mc[nt][0] - mx0), pow2i(Mc[nt][1] - mx1));
           unit = unit && (mx0 == Mc[nt][0]) && (mx1 == Mc[nt][1]);
           Mc[nt][0] = mx0;
           Mc[nt][1] = mx1;
@@ -393,9 +444,18 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
               float2 x1 = __fmul2_rn(make_float2(O[m][nt][2], O[m][nt][3]), a2[nt]);
               O[m][nt][0] = x0.x; O[m][nt][1] = x0.y; O[m][nt][2] = x1.x; O[m][nt][3] = x1.y;
             }
+          if constexpr (FOLD) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              Oc[nt][0] *= a2[nt].x; Oc[nt][1] *= a2[nt].y;
+              Oc[nt][2] *= a2[nt].x; Oc[nt][3] *= a2[nt].y;
+            }
+          }
         }
-        // P fragment factors 2^(m_q - M) for the fragment column row 8nt + r.
+        // P fragment factors 2^(m_q - M) for the fragment column row 8nt + r
+        // (times 2^Ex for the folded rule's packed blocks).
         uint32_t fb[TEAM_WARPS][NT];
+        float fs[TEAM_WARPS][NT];
         bool same = true;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -406,19 +466,42 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
             mq[w] = ms[w * C::ROWS + 8 * nt + r];
             mx = fmaxf(mx, mq[w]);
           }
+          if constexpr (FOLD) Ls[nt] = __fmul2_rn(Ls[nt], make_float2(pow2s(Mb[nt] - mx + dE), pow2s(Mb[nt] - mx + dE)));
           Mb[nt] = mx;
 #pragma unroll
           for (int w = 0; w < TEAM_WARPS; ++w) {
             const float f = pow2i(mq[w] - mx);
             same = same && mq[w] == mx;
             fb[w][nt] = Elem<DT>::pack2(f, f);
+            if constexpr (FOLD) fs[w][nt] = pow2s(mq[w] - mx + Ex);
           }
         }
         const bool scaled = !__all_sync(0xffffffffu, same);
-        const uint8_t *vst = smem + C::OFF_V + sv * C::VST;
         const uint8_t *pb = smem + C::OFF_P + (team * 2 + par) * C::ROWS * PP;
-        if (pk) pw.packed(vst, pb, O, fb, scaled);
-        else pw.resid(vst, pb, O, fb, scaled);
+        if (pk) {
+          if constexpr (FOLD) pw.packed_fold(sbase + C::OFF_V + sv * C::VST, vst, pb, O, Oc, Ls, fs);
+          else pw.packed(vst, pb, O, fb, scaled);
+        } else if constexpr (FOLD) {
+          // The exact window at the accumulator's scale 2^Ex: bring the
+          // accumulator to scale 1 around the 16-bit MMAs (fb <= 1 keeps P
+          // in range for fp16 queries).
+          const float down = pow2s(float(-Ex)), up = pow2s(float(Ex));
+#pragma unroll
+          for (int m = 0; m < C::MTV; ++m)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) O[m][nt][c] *= down;
+          pw.resid_fold(vst, pb, O, fb, scaled);
+#pragma unroll
+          for (int m = 0; m < C::MTV; ++m)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) O[m][nt][c] *= up;
+        } else {
+          pw.resid(vst, pb, O, fb, scaled);
+        }
       }
       mbar_arrive(bar(VEMPTY + sv));
       mbar_arrive(bar(PEMPTY + team * 2 + par));
@@ -458,16 +541,40 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   } else if (warp < PRODUCER) {
     const int c = (warp - QK_WARPS) % TEAM_WARPS;
     float *rt = red + team * C::ROWS * D;
+    if constexpr (FOLD) {
+      // O = ((accumulator - offset) / (1 or 16) + sum p f low) / 2^Ex, in the
+      // team's common softmax scale.
+      PvWarp<BITS, D, NT, DT, FOLD> pw;
+      pw.lane = lane; pw.r = r; pw.qd = qd; pw.c = c;
+      const float down = pow2s(float(-Ex));
 #pragma unroll
-    for (int m = 0; m < C::MTV; ++m)
+      for (int nt = 0; nt < NT; ++nt) {
+        float L = Ls[nt].x + Ls[nt].y;
+        L += __shfl_xor_sync(0xffffffffu, L, 1);
+        L += __shfl_xor_sync(0xffffffffu, L, 2);
+        const float L0 = __shfl_sync(0xffffffffu, L, 8 * qd);
+        const float L1 = __shfl_sync(0xffffffffu, L, 8 * qd + 4);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+        for (int m = 0; m < C::MTV; ++m)
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int row = 8 * nt + 2 * qd + (cc & 1);
-          const int ch = (D / 4) * c + C::CPL * r + 2 * m + (cc >> 1);
-          rt[row * D + ch] = O[m][nt][cc];
-        }
+          for (int cc = 0; cc < 4; ++cc) {
+            const int row = 8 * nt + 2 * qd + (cc & 1);
+            const float v = (O[m][nt][cc] - Oc[nt][cc & 1]) * pw.fold_inv(cc) + ((cc & 1) ? L1 : L0);
+            rt[row * D + pw.fold_channel(m, cc)] = v * down;
+          }
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < C::MTV; ++m)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int row = 8 * nt + 2 * qd + (cc & 1);
+            const int ch = (D / 4) * c + C::CPL * r + 2 * m + (cc >> 1);
+            rt[row * D + ch] = O[m][nt][cc];
+          }
+    }
     if (c == 0 && r == 0) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -912,10 +1019,10 @@ int cached_maps(const ckv_seq &s, int hkv, SeqDev &d) {
   return CKV_OK;
 }
 
-template <int BITS, int D, int NT, int DT, int MAXS>
+template <int BITS, int D, int NT, int DT, int MAXS, bool FOLD>
 int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
-  using C = Cfg<BITS, D, NT>;
-  auto kern = attn_kernel<BITS, D, NT, DT, MAXS>;
+  using C = Cfg<BITS, D, NT, FOLD>;
+  auto kern = attn_kernel<BITS, D, NT, DT, MAXS, FOLD>;
   // The shared-memory attribute belongs to the device's context: set once
   // per context (a cudaDeviceReset gives the device a new one).
   static std::atomic<unsigned long long> configured[64];
@@ -976,15 +1083,24 @@ int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st)
   return CKV_OK;
 }
 
-template <int BITS, int D, int NT, int DT>
+template <int BITS, int D, int NT, int DT, bool FOLD>
 int dispatch_seqs(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
-  return a.num_seqs == 1 ? launch<BITS, D, NT, DT, 1>(a, pl, ws, st)
-                         : launch<BITS, D, NT, DT, CKV_MAX_SEQS>(a, pl, ws, st);
+  return a.num_seqs == 1 ? launch<BITS, D, NT, DT, 1, FOLD>(a, pl, ws, st)
+                         : launch<BITS, D, NT, DT, CKV_MAX_SEQS, FOLD>(a, pl, ws, st);
+}
+// The folded rule covers D = 128 and 256 (each value warp's channels fill
+// whole 16-byte chunks of the stage rows).
+template <int BITS, int D, int NT, int DT>
+int dispatch_fold(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
+  if constexpr (D >= 128) {
+    if (a.flags & CKV_DEQUANT_FOLDED) return dispatch_seqs<BITS, D, NT, DT, true>(a, pl, ws, st);
+  }
+  return dispatch_seqs<BITS, D, NT, DT, false>(a, pl, ws, st);
 }
 template <int BITS, int D, int NT>
 int dispatch_dt(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
-  return a.dtype == CKV_BF16 ? dispatch_seqs<BITS, D, NT, CKV_BF16>(a, pl, ws, st)
-                             : dispatch_seqs<BITS, D, NT, CKV_F16>(a, pl, ws, st);
+  return a.dtype == CKV_BF16 ? dispatch_fold<BITS, D, NT, CKV_BF16>(a, pl, ws, st)
+                             : dispatch_fold<BITS, D, NT, CKV_F16>(a, pl, ws, st);
 }
 template <int BITS, int D>
 int dispatch_nt(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
@@ -1026,7 +1142,7 @@ extern "C" int ckv_attention(const ckv_attn_args *args, void *workspace, size_t 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   if (!(args->flags & CKV_WS_COUNTERS_ZERO))
-    CKV_CUDA_TRY(cudaMemsetAsync(ws, 0, kCounterOff + size_t(args->num_seqs) * args->heads_kv * 4, st));
+    CKV_CUDA_TRY(cudaMemsetAsync(ws, 0, kCounterBytes, st));
   return args->bits == 8 ? dispatch_d<8>(*args, pl, ws, st) : dispatch_d<4>(*args, pl, ws, st);
 }
 

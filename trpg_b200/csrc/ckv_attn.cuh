@@ -109,7 +109,9 @@ constexpr int align1k(int x) { return (x + 1023) / 1024 * 1024; }
 __host__ __device__ constexpr int ml_stride(int rows) { return (rows * 2 + 3) & ~3; }
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
-template <int BITS, int D, int NT>
+// FOLD selects the folded dequantization (see QkWarp::packed_fold and
+// PvWarp::packed_fold); false is the exact per-element rule.
+template <int BITS, int D, int NT, bool FOLD = false>
 struct Cfg {
   static constexpr int ROWS = 8 * NT;                   // query rows incl. padding
   // K stage: codes [D][SB] (one row per channel, 128 tokens) then (scale, low)[D].
@@ -130,7 +132,7 @@ struct Cfg {
   static constexpr int VCODE = 128 * VROWB;
   static constexpr int VMETA = 128 * NG * 8;
   static constexpr int VST = align1k(cmax(VCODE + VMETA, RBYTES));
-  static constexpr int NV = NT == 1 ? 3 : 2;            // V stage ring depth
+  static constexpr int NV = (NT == 1 && !FOLD) ? 3 : 2; // V stage ring depth
   // QK: each warp covers all D channels in KQS k-steps of 16.
   static constexpr int KQS = D / 16;
   // PV: each warp covers D/4 channels, CPL per lane, MTV m-tiles.
@@ -139,8 +141,11 @@ struct Cfg {
   // Shared-memory map (offsets from a 1024-byte aligned base).
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + NK * KST;
-  static constexpr int OFF_Q = OFF_V + NV * VST;                   // [KQS][NT][32] query B fragments
-  static constexpr int OFF_P = OFF_Q + KQS * NT * 32 * 8;          // [TEAMS][2][ROWS][PP]
+  // Query fragments per (k-step, n-tile, lane): two 16-bit pairs (8 bytes,
+  // exact rule) or the four channels' fp32 values (16 bytes, folded rule).
+  static constexpr int QFRAG = FOLD ? 16 : 8;
+  static constexpr int OFF_Q = OFF_V + NV * VST;                   // [KQS][NT][32] query fragments
+  static constexpr int OFF_P = OFF_Q + KQS * NT * 32 * QFRAG;      // [TEAMS][2][ROWS][PP]
   static constexpr int OFF_XM = OFF_P + TEAMS * 2 * ROWS * PP;     // [TEAMS][2][4][ROWS] P scales m_q
   static constexpr int OFF_END = OFF_XM + TEAMS * 2 * TEAM_WARPS * ROWS * 4;
   static constexpr int SMEM = OFF_END + 1024;                      // + alignment slack
@@ -181,6 +186,44 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr)
                : "memory");
+}
+
+// Four 8x8 matrices of 16-bit elements, transposed on the way into registers
+// (lane 4r + qd receives rows 2qd and 2qd + 1 of column r of each matrix).
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// Two fp32 values -> fp16 pair (`lo` in the low half), rounded to nearest,
+// saturating at the largest finite fp16 instead of overflowing to inf.
+__device__ __forceinline__ uint32_t f16x2_sat(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// fp16 pair (1024, 1024): the constant operand that measures the offset of
+// the exponent-bias conversion below.
+constexpr uint32_t kF16Pair1024 = 0x64006400u;
+
+// Bytes 0 and 2 (kLo) or 1 and 3 (kHi) of w as the fp16 pair (1024 + byte):
+// the byte becomes the low mantissa bits under the exponent of 1024 (the
+// exponent-bias conversion of Kim et al., "Who Says Elephants Can't Run",
+// 2022).  One PRMT per two codes.
+constexpr uint32_t kSelLo = 0x4240u, kSelHi = 0x4341u;
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t byte_pair_f16(uint32_t w) {
+  return prmt(w, 0x64646464u, SEL);
+}
+// The same for 4-bit codes: nibble 0 (T = 0), 1, 2 or 3 of bytes 0 and 2
+// as (1024 + code) for even T and (1024 + 16 code) for odd T.
+template <int T>
+__device__ __forceinline__ uint32_t nib_pair_f16(uint32_t w) {
+  const uint32_t v = T >= 2 ? (w >> 8) : w;
+  return (v & ((T & 1) ? 0x00F000F0u : 0x000F000Fu)) | kF16Pair1024;
 }
 
 // 2^d for an integer-valued d <= 0; 0 below the normal range and for -inf
@@ -227,15 +270,134 @@ __device__ __forceinline__ uint32_t swz_col(int row_rep, int col) {
 // ---------------------------------------------------------------------------
 // QK warp: partial logits of one item over half of the channels.
 // ---------------------------------------------------------------------------
-template <int BITS, int D, int NT, int DT>
+template <int BITS, int D, int NT, int DT, bool FOLD = false>
 struct QkWarp {
-  using C = Cfg<BITS, D, NT>;
+  using C = Cfg<BITS, D, NT, FOLD>;
   using E = Elem<DT>;
   int lane, r, qd, q;
-  const uint8_t *qfr;   // query B fragments [KQS][NT][32] (shared memory)
+  const uint8_t *qfr;   // query fragments [KQS][NT][32] (shared memory)
 
+  // B fragment of the query (16-bit pairs): channels 16s + 2qd, +1 and
+  // 16s + 2qd + 8, +9 of query row 8nt + r.
   __device__ __forceinline__ uint2 qfrag(int s, int nt) const {
-    return lds<uint2>(qfr, ((s * NT + nt) * 32 + lane) * 8);
+    if constexpr (FOLD) {
+      const float4 v = lds<float4>(qfr, ((s * NT + nt) * 32 + lane) * 16);
+      return make_uint2(E::pack2(v.x, v.y), E::pack2(v.z, v.w));
+    } else {
+      return lds<uint2>(qfr, ((s * NT + nt) * 32 + lane) * 8);
+    }
+  }
+
+  // Token (within the item) of logit S[mt][nt][2u + j] of a packed block.
+  __device__ __forceinline__ int packed_token(int mt, int u) const {
+    if constexpr (FOLD && BITS == 8) return 32 * q + 16 * mt + 2 * r + u;
+    return 32 * q + 4 * r + 2 * mt + u;
+  }
+
+  // Folded dequantization of one packed block's logits, for this warp's 32
+  // tokens.  With k = code * scale + low per (channel d, token t),
+  //   q.k_t = sum_d w_d code_dt + sum_d q_d low_d,   w_d = q_d scale_d,
+  // so the scales go into the query operand once per block instead of into
+  // every code.  The codes reach the tensor cores as exact fp16 values
+  // (1024 + code, or 1024 + 16 code for the odd 4-bit positions) straight
+  // from an ldmatrix.trans of the channel-major stage and one PRMT / LOP3 per
+  // two codes; w is rounded to fp16 (saturating); a second MMA with the
+  // constant operand 1024 gives the offset sum_d 1024 w_d, which is
+  // subtracted, and the low term is summed in fp32.  Same output layout as
+  // packed(): S[mt][nt][2u + j], token packed_token(mt, u), row 8nt + 2qd + j.
+  __device__ void packed_fold(uint32_t kst, const uint8_t *kst_ptr, float (&S)[2][NT][4]) const {
+    float corr[NT][4];
+    float2 clow[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        corr[nt][c] = 0.f;
+        S[0][nt][c] = S[1][nt][c] = 0.f;
+      }
+      clow[nt] = make_float2(0.f, 0.f);
+    }
+    const uint8_t *meta = kst_ptr + C::KCODE;
+    const uint32_t one[4] = {kF16Pair1024, kF16Pair1024, kF16Pair1024, kF16Pair1024};
+    // ldmatrix row addresses: lane 8m + i gives row i of matrix m.
+    const int m = lane >> 3, i = lane & 7;
+    uint32_t base;
+    if constexpr (BITS == 8) {
+      // Matrix m: channels 8(m & 1) + 0..7 of the k-step, tokens 32q + 16(m >> 1)
+      // + 0..15 (one 16-byte chunk of the 128-byte row, 128-byte swizzle).
+      base = kst + (8 * (m & 1) + i) * 128 + (((2 * q + (m >> 1)) ^ i) << 4);
+    } else {
+      // Matrix m: channels 8m + 0..7 of a pair of k-steps, this warp's 32
+      // tokens (chunk q of the 64-byte row, 64-byte swizzle: row bits [1, 3)).
+      base = kst + (8 * m + i) * 64 + ((q ^ (i >> 1)) << 4);
+    }
+    uint32_t x[4];
+#pragma unroll 4
+    for (int s = 0; s < C::KQS; ++s) {
+      const int cb = 16 * s + 2 * qd;   // channels cb, cb+1, cb+8, cb+9
+      const float4 m0 = lds<float4>(meta, cb * 8);          // (scale, low) of cb, cb + 1
+      const float4 m1 = lds<float4>(meta, (cb + 8) * 8);    // of cb + 8, cb + 9
+      uint32_t b[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float4 qv = lds<float4>(qfr, ((s * NT + nt) * 32 + lane) * 16);
+        const float2 w01 = __fmul2_rn(make_float2(qv.x, qv.y), make_float2(m0.x, m0.z));
+        const float2 w89 = __fmul2_rn(make_float2(qv.z, qv.w), make_float2(m1.x, m1.z));
+        b[nt][0] = f16x2_sat(w01.x, w01.y);
+        b[nt][1] = f16x2_sat(w89.x, w89.y);
+        clow[nt] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(m0.y, m0.w), clow[nt]);
+        clow[nt] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(m1.y, m1.w), clow[nt]);
+        mma16816<CKV_F16>(corr[nt], one, b[nt][0], b[nt][1]);
+      }
+      uint32_t a[2][4];
+      if constexpr (BITS == 8) {
+        ldmatrix_x4_trans(x, base + s * 16 * 128);
+        // x[2mt]: channels 2qd, 2qd+1 of the first 8, tokens 16mt + 2r, +1;
+        // x[2mt + 1]: the same for channels 8..15.
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          a[mt][0] = byte_pair_f16<kSelLo>(x[2 * mt]);        // row r: token 16mt + 2r
+          a[mt][1] = byte_pair_f16<kSelHi>(x[2 * mt]);        // row r + 8: token 16mt + 2r + 1
+          a[mt][2] = byte_pair_f16<kSelLo>(x[2 * mt + 1]);
+          a[mt][3] = byte_pair_f16<kSelHi>(x[2 * mt + 1]);
+        }
+      } else {
+        if ((s & 1) == 0) ldmatrix_x4_trans(x, base + (s >> 1) * 32 * 64);
+        // x[2(s & 1)]: channels 2qd, 2qd+1 of the first 8, tokens 4r..4r+3;
+        // x[2(s & 1) + 1]: the same for channels 8..15.
+        const uint32_t x0 = x[2 * (s & 1)], x1 = x[2 * (s & 1) + 1];
+        a[0][0] = nib_pair_f16<0>(x0);   // row r: token 4r
+        a[0][1] = nib_pair_f16<1>(x0);   // row r + 8: token 4r + 1 (x16)
+        a[0][2] = nib_pair_f16<0>(x1);
+        a[0][3] = nib_pair_f16<1>(x1);
+        a[1][0] = nib_pair_f16<2>(x0);   // row r: token 4r + 2
+        a[1][1] = nib_pair_f16<3>(x0);   // row r + 8: token 4r + 3 (x16)
+        a[1][2] = nib_pair_f16<2>(x1);
+        a[1][3] = nib_pair_f16<3>(x1);
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<CKV_F16>(S[mt][nt], a[mt], b[nt][0], b[nt][1]);
+    }
+    // sum_d q_d low_d per row: this lane holds part of row 8nt + r's sum; the
+    // logits of rows 8nt + 2qd + j need the whole sum of those rows.
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float c = clow[nt].x + clow[nt].y;
+      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      c += __shfl_xor_sync(0xffffffffu, c, 2);
+      const float c0 = __shfl_sync(0xffffffffu, c, 8 * qd);
+      const float c1 = __shfl_sync(0xffffffffu, c, 8 * qd + 4);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float f = (BITS == 4 && u == 1) ? 0.0625f : 1.f;
+          S[mt][nt][2 * u] = (S[mt][nt][2 * u] - corr[nt][0]) * f + c0;
+          S[mt][nt][2 * u + 1] = (S[mt][nt][2 * u + 1] - corr[nt][1]) * f + c1;
+        }
+    }
   }
 
   // S[mt][nt][c]: tokens 32q + 4r + 2mt (c = 0, 1) and 32q + 4r + 2mt + 1
@@ -330,11 +492,185 @@ struct QkWarp {
 // PV warp: O += P.V over one item's token half and channel quarter.
 // O[i][nt][c]: channel (D/4)c + CPL r + 2i + (c >> 1), query row 8nt + 2qd + (c & 1).
 // ---------------------------------------------------------------------------
-template <int BITS, int D, int NT, int DT>
+template <int BITS, int D, int NT, int DT, bool FOLD = false>
 struct PvWarp {
-  using C = Cfg<BITS, D, NT>;
+  using C = Cfg<BITS, D, NT, FOLD>;
   using E = Elem<DT>;
   int lane, r, qd, c;
+
+  // ---- folded dequantization ------------------------------------------------
+  // With v = code * scale_t + low_t per (token t, 64-channel group),
+  //   sum_t p_t v_t = sum_t (p_t scale_t) code_t + sum_t p_t low_t,
+  // so the per-token scale goes into the probability operand: P'' = fp16(p f
+  // scale_t), with f = 2^(m_q - M + E) (the softmax rescale of the QK warp
+  // that wrote p, and this warp's range exponent E).  The codes reach the
+  // tensor cores as exact fp16 values (1024 + code, 1024 + 16 code for odd
+  // 4-bit channels) from an ldmatrix.trans of the token-major stage; a second
+  // MMA with the constant 1024 measures the offset (Oc), and sum_t p_t f low_t
+  // (Ls) is summed in fp32.  This warp's channels lie in one group.
+  //
+  // O[i][nt][cc]: channel fold_channel(i, cc), query row 8nt + 2qd + (cc & 1).
+  static constexpr int CHUNKS = (D / 4) * BITS / 8 / 16;   // 16-byte chunks of this warp's channels
+
+  __device__ __forceinline__ int fold_channel(int i, int cc) const {
+    if constexpr (BITS == 8) return (D / 4) * c + 16 * i + 2 * r + (cc >> 1);
+    return (D / 4) * c + 32 * (i >> 1) + 4 * r + 2 * (i & 1) + (cc >> 1);
+  }
+  // 1 / 16 for the odd 4-bit channels (their codes arrive as 1024 + 16 code).
+  __device__ __forceinline__ static constexpr float fold_inv(int cc) {
+    return (BITS == 4 && (cc >> 1)) ? 0.0625f : 1.f;
+  }
+
+  // Largest scale of this warp's group over the stage's 128 tokens (all lanes).
+  __device__ float fold_scale_max(const uint8_t *vst) const {
+    const int grp = ((D / 4) * c) / 64;
+    const uint8_t *meta = vst + C::VCODE;
+    float mx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mx = fmaxf(mx, lds<float>(meta, ((lane + 32 * k) * C::NG + grp) * 8));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    return mx;
+  }
+
+  // ldmatrix row address of this lane in the stage for token row `row0`
+  // (a multiple of 16) and 16-byte chunk `chunk` of this warp's bytes.
+  __device__ __forceinline__ uint32_t fold_addr(uint32_t vst, int row, int chunk) const {
+    const int off = ((D / 4) * c) * BITS / 8 + 16 * chunk;   // byte of the chunk in a token row
+    const int box = off / C::VBOX, inb = off % C::VBOX;
+    const uint32_t a = uint32_t(row * C::VBOX + inb);
+    return vst + box * 128 * C::VBOX + swz<C::VSWZ>(a);
+  }
+
+  // Exact-window chunk in the folded accumulator layout: the same 16-bit MMA
+  // as resid(), with m-tile i's rows on channels fold_channel(i, 0) and
+  // fold_channel(i, 2) (= + 1), and the odd 4-bit channels' values times 16
+  // (their packed accumulators are in that scale).
+  __device__ void resid_fold(const uint8_t *vst, const uint8_t *pb, float (&O)[C::MTV][NT][4],
+                             const uint32_t (&fb)[TEAM_WARPS][NT], bool scaled) const {
+    const uint32_t sixteen = BITS == 4 ? E::pack2(16.f, 16.f) : 0u;
+#pragma unroll
+    for (int j = 0; j < RCHUNK / 16; ++j) {
+      const int t0 = 16 * j + 2 * qd;
+      uint2 b[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        b[nt] = lds<uint2>(pb, (8 * nt + r) * PP + (16 * j + 4 * qd) * 2);
+        if (scaled) {
+          b[nt].x = E::mul2(b[nt].x, fb[j][nt]);
+          b[nt].y = E::mul2(b[nt].y, fb[j][nt]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < C::MTV; ++i) {
+        const uint32_t coff = uint32_t(fold_channel(i, 0)) * 2;
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = lds<uint32_t>(vst, (t0 + (e & 1) + 8 * (e >> 1)) * C::RP + coff);
+        uint32_t a[4];
+        a[0] = prmt(w[0], w[1], 0x5410u);   // row r: channel fold_channel(i, 0), tokens t0, t0 + 1
+        a[1] = prmt(w[0], w[1], 0x7632u);   // row r + 8: the next channel
+        a[2] = prmt(w[2], w[3], 0x5410u);
+        a[3] = prmt(w[2], w[3], 0x7632u);
+        if constexpr (BITS == 4) {
+          a[1] = E::mul2(a[1], sixteen);
+          a[3] = E::mul2(a[3], sixteen);
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<DT>(O[i][nt], a, b[nt].x, b[nt].y);
+      }
+    }
+  }
+
+  __device__ void packed_fold(uint32_t vst, const uint8_t *vst_ptr, const uint8_t *pb,
+                              float (&O)[C::MTV][NT][4], float (&Oc)[NT][4], float2 (&Ls)[NT],
+                              const float (&fs)[TEAM_WARPS][NT]) const {
+    const int grp = ((D / 4) * c) / 64;
+    const uint8_t *meta = vst_ptr + C::VCODE + grp * 8;
+    const uint8_t *prow = pb + r * PP + 4 * qd * 2;
+    const uint32_t one[4] = {kF16Pair1024, kF16Pair1024, kF16Pair1024, kF16Pair1024};
+    const int m = lane >> 3, i = lane & 7;
+    // Matrix m of the x4 loads: token rows 8(m & 1) + i of the k-step, chunk
+    // (m >> 1) of the pair of chunks the load covers.
+    uint32_t addr[C::MTV >= 2 ? 2 : 1];
+    if constexpr (BITS == 8) {
+#pragma unroll
+      for (int k = 0; k < CHUNKS / 2; ++k) addr[k] = fold_addr(vst, 8 * (m & 1) + i, 2 * k + (m >> 1));
+    } else if constexpr (CHUNKS == 2) {
+      addr[0] = fold_addr(vst, 8 * (m & 1) + i, m >> 1);
+    } else {
+      // One chunk: the x4 load covers two k-steps (matrix m: k-step m >> 1).
+      addr[0] = fold_addr(vst, 16 * (m >> 1) + 8 * (m & 1) + i, 0);
+    }
+    uint32_t x[CHUNKS / 2 > 0 ? 2 * CHUNKS : 4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t0 = 16 * j + 2 * qd;   // tokens t0, t0+1, t0+8, t0+9
+      const float2 s0 = lds<float2>(meta, (t0 * C::NG) * 8);
+      const float2 s1 = lds<float2>(meta, ((t0 + 1) * C::NG) * 8);
+      const float2 s8 = lds<float2>(meta, ((t0 + 8) * C::NG) * 8);
+      const float2 s9 = lds<float2>(meta, ((t0 + 9) * C::NG) * 8);
+      uint32_t b[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 pv = lds<uint2>(prow, 8 * nt * PP + 32 * j);
+        const float f = fs[j >> 1][nt];
+        const float2 p01 = __fmul2_rn(E::unpack2(pv.x), make_float2(f, f));
+        const float2 p89 = __fmul2_rn(E::unpack2(pv.y), make_float2(f, f));
+        const float2 w01 = __fmul2_rn(p01, make_float2(s0.x, s1.x));
+        const float2 w89 = __fmul2_rn(p89, make_float2(s8.x, s9.x));
+        b[nt][0] = f16x2_sat(w01.x, w01.y);
+        b[nt][1] = f16x2_sat(w89.x, w89.y);
+        Ls[nt] = __ffma2_rn(p01, make_float2(s0.y, s1.y), Ls[nt]);
+        Ls[nt] = __ffma2_rn(p89, make_float2(s8.y, s9.y), Ls[nt]);
+        mma16816<CKV_F16>(Oc[nt], one, b[nt][0], b[nt][1]);
+      }
+      if constexpr (BITS == 8) {
+#pragma unroll
+        for (int k = 0; k < CHUNKS / 2; ++k) {
+          uint32_t y[4];
+          ldmatrix_x4_trans(y, addr[k] + j * 16 * C::VBOX);
+          // y[2e]: chunk 2k + e, tokens t0, t0 + 1; y[2e + 1]: tokens t0 + 8, + 9.
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            uint32_t a[4];
+            a[0] = byte_pair_f16<kSelLo>(y[2 * e]);       // row r: channel 2r of the chunk
+            a[1] = byte_pair_f16<kSelHi>(y[2 * e]);       // row r + 8: channel 2r + 1
+            a[2] = byte_pair_f16<kSelLo>(y[2 * e + 1]);
+            a[3] = byte_pair_f16<kSelHi>(y[2 * e + 1]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma16816<CKV_F16>(O[2 * k + e][nt], a, b[nt][0], b[nt][1]);
+          }
+        }
+      } else {
+        uint32_t lo[CHUNKS], hi[CHUNKS];   // per chunk: tokens t0, t0+1 and t0+8, t0+9
+        if constexpr (CHUNKS == 2) {
+          ldmatrix_x4_trans(x, addr[0] + j * 16 * C::VBOX);
+          lo[0] = x[0]; hi[0] = x[1]; lo[1] = x[2]; hi[1] = x[3];
+        } else {
+          if ((j & 1) == 0) ldmatrix_x4_trans(x, addr[0] + j * 16 * C::VBOX);
+          lo[0] = x[2 * (j & 1)]; hi[0] = x[2 * (j & 1) + 1];
+        }
+#pragma unroll
+        for (int k = 0; k < CHUNKS; ++k) {
+          uint32_t a0[4], a1[4];
+          a0[0] = nib_pair_f16<0>(lo[k]);   // row r: channel 4r
+          a0[1] = nib_pair_f16<1>(lo[k]);   // row r + 8: channel 4r + 1 (x16)
+          a0[2] = nib_pair_f16<0>(hi[k]);
+          a0[3] = nib_pair_f16<1>(hi[k]);
+          a1[0] = nib_pair_f16<2>(lo[k]);   // row r: channel 4r + 2
+          a1[1] = nib_pair_f16<3>(lo[k]);   // row r + 8: channel 4r + 3 (x16)
+          a1[2] = nib_pair_f16<2>(hi[k]);
+          a1[3] = nib_pair_f16<3>(hi[k]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            mma16816<CKV_F16>(O[2 * k][nt], a0, b[nt][0], b[nt][1]);
+            mma16816<CKV_F16>(O[2 * k + 1][nt], a1, b[nt][0], b[nt][1]);
+          }
+        }
+      }
+    }
+  }
 
   // fb[q][nt]: packed factor pair for the P fragments written by QK warp q
   // (applied when `scaled`).

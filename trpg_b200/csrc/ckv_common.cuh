@@ -46,6 +46,10 @@ template <> struct Elem<CKV_BF16> {
     asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
   }
+  // Packed pair -> (lo, hi) in fp32 (exact: bf16 is the top half of fp32).
+  __device__ static float2 unpack2(uint32_t v) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
 };
 template <> struct Elem<CKV_F16> {
   using T = __half;
@@ -60,6 +64,11 @@ template <> struct Elem<CKV_F16> {
     uint32_t r;
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
+  }
+  __device__ static float2 unpack2(uint32_t v) {
+    __half2 h;
+    memcpy(&h, &v, 4);
+    return __half22float2(h);
   }
 };
 

@@ -9,6 +9,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/library.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -352,6 +353,15 @@ ckv_seq make_seq(const Tensor &q, const Tensor &kd, const Tensor &km, const Tens
 void run_attention(std::vector<ckv_seq> &seqs, const Tensor &q0, int64_t hq, int64_t hkv, int64_t D,
                    int64_t nq, int64_t bits, double scale, bool partial);
 
+// Dequantization rule of the attention ops in this process: 0 exact (the
+// reference's per-element rounding), 1 folded (CKV_DEQUANT_FOLDED).
+std::atomic<int> g_dequant{0};
+
+int64_t set_dequant(int64_t mode) {
+  TORCH_CHECK(mode == 0 || mode == 1, "ckv::set_dequant: mode must be 0 (exact) or 1 (folded)");
+  return g_dequant.exchange(int(mode));
+}
+
 // queries[i]: [1,Hq,nq,D]; banks and residuals per sequence; ranges[i*4..] =
 // (unit_begin, unit_end, resid_begin, resid_end).  Returns one tensor per
 // sequence: [1,Hq,nq,D] in the query dtype, or [Hq*nq, D+2] fp32 partials.
@@ -424,7 +434,7 @@ void run_attention(std::vector<ckv_seq> &seqs, const Tensor &q0, int64_t hq, int
   a.dtype = dtype_code(q0.scalar_type());
   a.scale = float(scale);
   a.partial = partial ? 1 : 0;
-  a.flags = CKV_WS_COUNTERS_ZERO;
+  a.flags = CKV_WS_COUNTERS_ZERO | (g_dequant.load(std::memory_order_relaxed) ? CKV_DEQUANT_FOLDED : 0);
   size_t bytes = 0;
   check_status(ckv_attention_workspace(&a, &bytes), "attention_workspace");
   Tensor ws = workspace_for(q0, bytes);
@@ -651,6 +661,7 @@ TORCH_LIBRARY(ckv, m) {
         "int offset) -> (Tensor(a), Tensor(b))");
   m.def("window_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
         "int capacity) -> (Tensor(a), Tensor(b))");
+  m.def("set_dequant(int mode) -> int", &set_dequant);
 }
 
 namespace {
