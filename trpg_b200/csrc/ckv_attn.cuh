@@ -797,5 +797,168 @@ struct PvWarp {
   }
 };
 
+
+// Bounded wait on an mbarrier phase that also gives up as soon as another
+// warp of the CTA has flagged an abort.  Returns false on either.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort || clock64() - start > (1ll << 31)) return false;
+  }
+  return true;
+}
+
+// 2^d for an integer-valued d <= 127 (either sign); 0 below the normal range
+// and for -inf or NaN.
+__device__ __forceinline__ float pow2s(float d) {
+  return !(d >= -126.f) ? 0.f : __int_as_float((int(fminf(d, 127.f)) + 127) << 23);
+}
+
+// The last CTA of a (sequence, KV head) pair merges the pair's CTA records
+// (m, l and the unnormalised output per row, in the workspace) into the
+// output, or into the pair's partial record when p.partial.  `avail` bytes of
+// shared memory at smem / sbase are free; s_mbar holds two mbarriers.
+template <int D, int DT, int NTHREADS, int ROWSMAX, class P>
+__device__ void merge_pair_records(const P &p, const SeqDev &sd, uint8_t *smem, uint32_t sbase,
+                                   uint64_t *s_mbar, int avail, int seq, int head, int G, int nq,
+                                   int rows, int tid, int warp, int lane) {
+  const int mls = ml_stride(rows);
+  // ---- last CTA of the pair: merge the pair's CTA records -------------------
+  // The pair's records are consecutive in the workspace ([cph][rows][D] fp32,
+  // then [cph][mls] (m, l) pairs), so bulk copies bring them into the freed
+  // stage memory in a few large transfers (records in chunks of `mrec` when
+  // they do not all fit).  The (m, l) pairs arrive first on their own
+  // barrier, so the record weights are ready when the records land; every
+  // output float4 is then summed by `parts` threads over disjoint record
+  // ranges.
+  const int c0 = sd.cta_begin + head * sd.cph;
+  const int cph = sd.cph;
+  constexpr int D4 = D / 4;
+  const int AVAIL = avail;
+  const int outs = rows * D4;
+  const int parts = max(1, min(4, NTHREADS / outs));
+  const uint32_t rec_bytes = uint32_t(rows) * D * 4;
+  const uint32_t ml_bytes = uint32_t(cph) * mls * 4;                 // a multiple of 16
+  const uint32_t w_off = ml_bytes;                                     // [rows][cph] weights
+  const uint32_t row_off = w_off + uint32_t(rows) * cph * 4;           // [ROWS] (M, L)
+  const uint32_t acc_off = (row_off + 2 * ROWSMAX * 4 + 15) & ~15u;    // [parts - 1][outs] float4
+  const uint32_t rec_off = (acc_off + uint32_t(parts - 1) * outs * 16 + 127) & ~127u;
+  const int mrec = max(1, min(cph, int((AVAIL - rec_off) / rec_bytes)));
+  const float2 *s_ml = reinterpret_cast<const float2 *>(smem);        // [cph][mls / 2]
+  float *s_w = reinterpret_cast<float *>(smem + w_off);
+  float *s_row = reinterpret_cast<float *>(smem + row_off);
+  float4 *s_acc = reinterpret_cast<float4 *>(smem + acc_off);
+  const float4 *s_rec = reinterpret_cast<const float4 *>(smem + rec_off);   // [mrec][rows][D4]
+  const uint32_t mbar_ml = smem_u32(&s_mbar[0]), mbar_rec = smem_u32(&s_mbar[1]);
+  auto issue_rec = [&](int cb, int cnt) {
+    mbar_expect_tx(mbar_rec, uint32_t(cnt) * rec_bytes);
+    bulk_load(sbase + rec_off, p.rec + size_t(c0 + cb) * rows * D, uint32_t(cnt) * rec_bytes, mbar_rec);
+  };
+  if (tid == 0) {
+    mbar_init(mbar_ml, 1);
+    mbar_init(mbar_rec, 1);
+    mbar_fence_init();
+    // The CTA's earlier generic writes to this shared memory and the acquired
+    // record stores of the other CTAs are ordered before the copies.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    mbar_expect_tx(mbar_ml, ml_bytes);
+    bulk_load(sbase, p.rec_ml + size_t(c0) * mls, ml_bytes, mbar_ml);
+    issue_rec(0, min(mrec, cph));
+  }
+  __syncthreads();
+  if (!mbar_wait(mbar_ml, 0)) atomicOr(p.error, 1u);
+  // Row maxima, record weights and the merged denominator.
+  for (int row = warp; row < rows; row += NTHREADS / 32) {
+    float M = -INFINITY;
+    for (int c = lane; c < cph; c += 32) M = fmaxf(M, s_ml[c * (mls / 2) + row].x);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int c = lane; c < cph; c += 32) {
+      const float2 ml = s_ml[c * (mls / 2) + row];
+      const float wt = (ml.x == -INFINITY) ? 0.f : ex2(ml.x - M);
+      s_w[row * cph + c] = wt;
+      L += wt * ml.y;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) {
+      s_row[2 * row] = M;
+      s_row[2 * row + 1] = L;
+    }
+  }
+  __syncthreads();
+  // Work unit u = tid + k * NTHREADS: output float4 o = u % outs, record part
+  // u / outs (k < 2 covers the largest case, 16 rows x 64 float4s, parts 1).
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  for (int cb = 0, chunk = 0; cb < cph; cb += mrec, ++chunk) {
+    const int cnt = min(mrec, cph - cb);
+    if (chunk > 0) {
+      __syncthreads();   // the previous chunk is consumed
+      if (tid == 0) issue_rec(cb, cnt);
+    }
+    if (!mbar_wait(mbar_rec, chunk & 1)) atomicOr(p.error, 1u);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int u = tid + k * NTHREADS;
+      if (u < outs * parts) {
+        const int o = u % outs, part = u / outs;
+        const int cl = part * cnt / parts, ce = (part + 1) * cnt / parts;
+        const float *wr = s_w + (o / D4) * cph + cb;
+        const float4 *src = s_rec + o;
+        float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+        int c = cl;
+        for (; c + 2 <= ce; c += 2) {
+          const float w0 = wr[c], w1 = wr[c + 1];
+          const float4 v0 = src[size_t(c) * outs], v1 = src[size_t(c + 1) * outs];
+          a0.x += w0 * v0.x; a0.y += w0 * v0.y; a0.z += w0 * v0.z; a0.w += w0 * v0.w;
+          a1.x += w1 * v1.x; a1.y += w1 * v1.y; a1.z += w1 * v1.z; a1.w += w1 * v1.w;
+        }
+        if (c < ce) {
+          const float w0 = wr[c];
+          const float4 v0 = src[size_t(c) * outs];
+          a0.x += w0 * v0.x; a0.y += w0 * v0.y; a0.z += w0 * v0.z; a0.w += w0 * v0.w;
+        }
+        acc[k].x += a0.x + a1.x; acc[k].y += a0.y + a1.y; acc[k].z += a0.z + a1.z; acc[k].w += a0.w + a1.w;
+      }
+    }
+  }
+  if (parts > 1) {
+    if (tid >= outs && tid < outs * parts) s_acc[tid - outs] = acc[0];
+    __syncthreads();
+    if (tid < outs)
+      for (int pp = 1; pp < parts; ++pp) {
+        const float4 v = s_acc[(pp - 1) * outs + tid];
+        acc[0].x += v.x; acc[0].y += v.y; acc[0].z += v.z; acc[0].w += v.w;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int o = tid + k * NTHREADS;
+    if (o >= outs || (parts > 1 && k > 0)) continue;
+    const int row = o / D4, d4 = o % D4;
+    const float M = s_row[2 * row], L = s_row[2 * row + 1];
+    const int nn = row / G, g = row % G;
+    const int64_t orow = int64_t(head * G + g) * nq + nn;
+    if (p.partial) {
+      float *out = static_cast<float *>(sd.out) + orow * (D + 2);
+      out[4 * d4] = acc[k].x; out[4 * d4 + 1] = acc[k].y; out[4 * d4 + 2] = acc[k].z; out[4 * d4 + 3] = acc[k].w;
+      if (d4 == 0) {
+        out[D] = M;
+        out[D + 1] = L;
+      }
+    } else {
+      typename Elem<DT>::T *out = static_cast<typename Elem<DT>::T *>(sd.out) + orow * D + 4 * d4;
+      const float inv = 1.f / L;
+      out[0] = Elem<DT>::from_f32(acc[k].x * inv);
+      out[1] = Elem<DT>::from_f32(acc[k].y * inv);
+      out[2] = Elem<DT>::from_f32(acc[k].z * inv);
+      out[3] = Elem<DT>::from_f32(acc[k].w * inv);
+    }
+  }
+  if (tid == 0) p.counters[seq * p.hkv + head] = 0u;
+}
 }  // namespace attn
 }  // namespace ckv

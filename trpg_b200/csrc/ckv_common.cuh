@@ -175,13 +175,18 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// One bounded try: the thread is suspended until the phase completes or
+// kSuspendNs nanoseconds pass, whichever is first, so a waiting warp issues
+// no instructions while it waits (a wake-up on completion is immediate; the
+// hint only caps the sleep).
+constexpr uint32_t kSuspendNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(done)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return done != 0;
 }
