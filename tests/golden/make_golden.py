@@ -122,4 +122,6 @@ def main(reference: str):
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    if len(sys.argv) != 2:
+        sys.exit('usage: python tests/golden/make_golden.py REFERENCE_SOURCE_TREE')
+    main(sys.argv[1])

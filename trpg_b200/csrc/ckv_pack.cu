@@ -99,102 +99,113 @@ __global__ void __launch_bounds__(256) unpack_rows_kernel(const uint8_t *__restr
   out[i] = E::from_f32(__fmaf_rn(float(code), m.x, m.y));
 }
 
-// Direct-to-slab append.  Grid: (blocks of 128 tokens, heads).  Block 256
-// threads.  Key part: thread c < D quantizes channel c over the block's 128
-// tokens.  Value part: thread t quantizes token t's groups.
+// Direct-to-slab append.  Grid: (blocks of 128 tokens x D/32 slices, heads);
+// block 256 threads.  Slice s of a block covers
+//   keys:   channels 32s..32s+31 over the block's 128 tokens -- thread
+//           (channel c = tid % 32, part = tid / 32) takes tokens 16 part..+15
+//           of channel c, the eight parts meet in shared memory for the
+//           channel's (min, max), and each part writes its 16 codes;
+//   values: the 64 (token, 64-channel group) rows of tokens
+//           (128 / (D/32)) s.. of the block -- four threads per row, 16
+//           channels each, (min, max) over the four by shuffles.
+// Every group's (min, max) is exact whatever the order of the comparisons,
+// so the codes match a one-thread-per-group quantizer bit for bit.
 template <int DT, int BITS, int D>
 __global__ void __launch_bounds__(256) append_kernel(ckv_append_args a) {
   using E = Elem<DT>;
   using T = typename E::T;
-  const int blk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  constexpr int SLICES = D / 32;
+  const int blk = blockIdx.x / SLICES, sl = blockIdx.x % SLICES, h = blockIdx.y, tid = threadIdx.x;
   const int64_t tok0 = int64_t(blk) * 128;
   const int unit = a.unit_offset + blk;
   const T *keys = static_cast<const T *>(a.keys) + h * a.k_stride_head + tok0 * a.k_stride_token;
   const T *values =
       static_cast<const T *>(a.values) + h * a.v_stride_head + tok0 * a.v_stride_token;
-  constexpr int KS = 128 * BITS / 8;  // key bytes per channel row
-  if (tid < D) {
-    const int c = tid;
-    float mn = INFINITY, mx = -INFINITY;
-    for (int t = 0; t < 128; ++t) {
-      float v = E::to_f32(keys[t * a.k_stride_token + c]);
-      mn = fminf(mn, v);
-      mx = fmaxf(mx, v);
+  __shared__ float2 part_mm[8][32];
+
+  // ---- keys: 32 channels x 128 tokens -------------------------------------
+  {
+    const int c = 32 * sl + (tid & 31), part = tid >> 5;
+    float v[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) v[t] = E::to_f32(keys[(16 * part + t) * a.k_stride_token + c]);
+    float mn = v[0], mx = v[0];
+#pragma unroll
+    for (int t = 1; t < 16; ++t) {
+      mn = fminf(mn, v[t]);
+      mx = fmaxf(mx, v[t]);
     }
-    float scale = group_scale<BITS>(mn, mx);
+    part_mm[part][tid & 31] = make_float2(mn, mx);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float2 m = part_mm[k][tid & 31];
+      mn = fminf(mn, m.x);
+      mx = fmaxf(mx, m.y);
+    }
+    const float scale = group_scale<BITS>(mn, mx);
+    constexpr int KS = 128 * BITS / 8;   // key bytes per channel row
     uint8_t *row = a.key_data + h * a.kd_stride_head + int64_t(unit) * a.kd_stride_unit + c * KS;
-    for (int i = 0; i < KS / 16; ++i) {
-      uint32_t w[4];
-      for (int k = 0; k < 4; ++k) {
-        uint32_t word = 0;
-        for (int b = 0; b < 4; ++b) {
-          int byte = i * 16 + k * 4 + b;
-          uint32_t val;
-          if constexpr (BITS == 8) {
-            val = quantize<8>(E::to_f32(keys[byte * a.k_stride_token + c]), mn, scale, a.rounding);
-          } else {
-            float x0 = E::to_f32(keys[(2 * byte) * a.k_stride_token + c]);
-            float x1 = E::to_f32(keys[(2 * byte + 1) * a.k_stride_token + c]);
-            val = quantize<4>(x0, mn, scale, a.rounding) |
-                  (quantize<4>(x1, mn, scale, a.rounding) << 4);
-          }
-          word |= val << (8 * b);
-        }
-        w[k] = word;
-      }
-      reinterpret_cast<uint4 *>(row)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if constexpr (BITS == 8) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) w[t >> 2] |= quantize<8>(v[t], mn, scale, a.rounding) << (8 * (t & 3));
+      reinterpret_cast<uint4 *>(row)[part] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) w[t >> 3] |= quantize<4>(v[t], mn, scale, a.rounding) << (4 * (t & 7));
+      reinterpret_cast<uint2 *>(row)[part] = make_uint2(w[0], w[1]);
     }
-    float *m = a.key_meta + h * a.km_stride_head + int64_t(unit) * a.km_stride_unit + c * 2;
-    reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+    if (part == 0) {
+      float *m = a.key_meta + h * a.km_stride_head + int64_t(unit) * a.km_stride_unit + c * 2;
+      reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+    }
   }
-  // Values: 128 tokens x D/64 groups per block; each thread handles whole
-  // groups of 64 contiguous channels.
-  constexpr int NG = D / 64;
-  constexpr int VB = 64 * BITS / 8;  // value bytes per group
-  for (int task = tid; task < 128 * NG; task += blockDim.x) {
-    const int t = task / NG, g = task % NG;
-    const uint4 *src = reinterpret_cast<const uint4 *>(values + t * a.v_stride_token + g * 64);
-    float v[64];
+
+  // ---- values: 64 (token, group) rows, four threads per row ----------------
+  {
+    constexpr int NG = D / 64;
+    constexpr int TPS = 128 / SLICES;     // tokens per slice
+    const int rowi = tid >> 2, q = tid & 3;
+    const int t = TPS * sl + rowi / NG, g = rowi % NG;
+    const uint4 *src = reinterpret_cast<const uint4 *>(values + t * a.v_stride_token + g * 64 + 16 * q);
+    float v[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint4 w = src[i];
-      const T *hv = reinterpret_cast<const T *>(&w);
+    for (int i = 0; i < 2; ++i) {
+      const uint4 wv = src[i];
+      const T *hv = reinterpret_cast<const T *>(&wv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[i * 8 + j] = E::to_f32(hv[j]);
+      for (int j = 0; j < 8; ++j) v[8 * i + j] = E::to_f32(hv[j]);
     }
     float mn = v[0], mx = v[0];
 #pragma unroll
-    for (int i = 1; i < 64; ++i) {
+    for (int i = 1; i < 16; ++i) {
       mn = fminf(mn, v[i]);
       mx = fmaxf(mx, v[i]);
     }
-    float scale = group_scale<BITS>(mn, mx);
-    const int64_t token = tok0 + t + int64_t(a.unit_offset) * 128;
-    uint8_t *dst = a.value_data + h * a.vd_stride_head + token * a.vd_stride_token + g * VB;
 #pragma unroll
-    for (int i = 0; i < VB / 16; ++i) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          int byte = i * 16 + k * 4 + b;
-          uint32_t val;
-          if constexpr (BITS == 8) {
-            val = quantize<8>(v[byte], mn, scale, a.rounding);
-          } else {
-            val = quantize<4>(v[2 * byte], mn, scale, a.rounding) |
-                  (quantize<4>(v[2 * byte + 1], mn, scale, a.rounding) << 4);
-          }
-          word |= val << (8 * b);
-        }
-        w[k] = word;
-      }
-      reinterpret_cast<uint4 *>(dst)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int o = 1; o < 4; o <<= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    float *m = a.value_meta + h * a.vm_stride_head + token * a.vm_stride_token + g * 2;
-    reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+    const float scale = group_scale<BITS>(mn, mx);
+    const int64_t token = tok0 + t + int64_t(a.unit_offset) * 128;
+    constexpr int VB = 64 * BITS / 8;   // value bytes per group
+    uint8_t *dst = a.value_data + h * a.vd_stride_head + token * a.vd_stride_token + g * VB;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if constexpr (BITS == 8) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i >> 2] |= quantize<8>(v[i], mn, scale, a.rounding) << (8 * (i & 3));
+      reinterpret_cast<uint4 *>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i >> 3] |= quantize<4>(v[i], mn, scale, a.rounding) << (4 * (i & 7));
+      reinterpret_cast<uint2 *>(dst)[q] = make_uint2(w[0], w[1]);
+    }
+    if (q == 0) {
+      float *m = a.value_meta + h * a.vm_stride_head + token * a.vm_stride_token + g * 2;
+      reinterpret_cast<float2 *>(m)[0] = make_float2(scale, mn);
+    }
   }
 }
 
@@ -248,7 +259,7 @@ int launch_unpack_rows(const uint8_t *codes, const float *meta, int64_t rows, in
 
 template <int DT, int BITS>
 int launch_append(const ckv_append_args &a, cudaStream_t s) {
-  dim3 grid(a.count / 128, a.heads);
+  dim3 grid(unsigned(a.count / 128 * (a.head_dim / 32)), unsigned(a.heads));
   switch (a.head_dim) {
     case 64: append_kernel<DT, BITS, 64><<<grid, 256, 0, s>>>(a); break;
     case 128: append_kernel<DT, BITS, 128><<<grid, 256, 0, s>>>(a); break;

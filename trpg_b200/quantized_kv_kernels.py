@@ -8,9 +8,16 @@ reference (``models/quantized_kv.py:16,29`` only routes CUDA tensors here).
 
 ``pack`` defaults to round-half-to-even with IEEE division, which reproduces
 the reference CPU quantizer (``models/quantized_kv.py:19-25``) bit for bit;
-``rounding='half_up'`` reproduces the tie rule of the reference Triton kernel
-(``models/quantized_kv_kernels.py:14``).  ``unpack`` rounds one fused
-multiply-add to ``dtype`` like the reference CUDA unpack (``:36``).
+``rounding='half_up'`` follows the tie rule of the reference Triton kernel
+(``floor(t + 0.5)``, ``models/quantized_kv_kernels.py:14``) with IEEE
+division.  It is pinned to fixtures that the reference's Triton kernel
+produced under the Triton interpreter on CPU, whose fp32 divide is IEEE;
+the same kernel compiled for a GPU may lower that divide differently and
+so differ where a quotient lies within an ulp of a rounding boundary.  No
+fixture from the compiled kernel exists: the reference's package install
+ships only its ``src/`` tree, so its ``models/`` kernels never reach a GPU
+host.  ``unpack`` rounds one fused multiply-add to ``dtype`` like the
+reference CUDA unpack (``:36``).
 """
 from __future__ import annotations
 
