@@ -270,6 +270,45 @@ def run_steps(seq, decode, steps, start=0, outs=None):
     return launches
 
 
+def capture_steps(seq, decode, count, inputs, stream, out):
+    """One CUDA graph per step position i < count of the rollback cycle, each
+    holding step i's 8 layers (append of the new key/value row into the
+    exact window, then decode) and the stack of the 8 outputs into `out`.
+
+    A serving loop replays the graph of the step it is at; the row a step
+    appends and the length it attends over are fixed per position, so the
+    graphs are captured in cycle order from the snapshot state and replaying
+    graph i reproduces step i of every cycle (graph 0 after graph count - 1
+    is the rollback).  ``inputs(i)`` gives step i's per-layer (q, k, v)."""
+    graphs = []
+    pool = torch.cuda.graph_pool_handle()
+    seq.rollback()
+    with torch.inference_mode():
+        for i in range(count):
+            qs, kns, vns = inputs(i)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, pool=pool):
+                outs = []
+                for li, layer in enumerate(seq.layers):
+                    view = layer.append_for_attention(kns[li], vns[li])
+                    outs.append(decode(qs[li], view, SCALE))
+                    layer.compact_residual()       # a no-op within the cycle
+                torch.stack(outs, out=out)
+            graphs.append(g)
+    seq.rollback()
+    return graphs
+
+
+def warm_stream(seq, decode, stream):
+    """One eager step on `stream` (its attention workspace is made outside
+    any capture), then back to the snapshot."""
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.inference_mode(), torch.cuda.stream(stream):
+        run_steps(seq, decode, 1)
+    stream.synchronize()
+    seq.rollback()
+
+
 def compaction_seconds(seq, repeats=8):
     """Device seconds of one layer's compaction (quantize 128 tokens into the
     banks and move the rest of the window), the work every 128th decode step
@@ -418,24 +457,61 @@ def b200_arm(args, world, rank, local):
     torch.cuda.set_device(device)
     clocks = Clocks(local)          # the sampler starts while the caches are built
     seq = Sequence(1000 + rank, args.steps + args.warmup, device)
-    # untimed warm-up
-    run_steps(seq, decode, args.warmup)
+    cycle = ROLLBACK - 1
+    count = min(cycle, max(args.steps, args.warmup))
+    stream = torch.cuda.Stream(device)
+    warm_stream(seq, decode, stream)
+    step_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16, device=device)
+    graphs = capture_steps(seq, decode, count, lambda i: (seq.qs[i], seq.kns[i], seq.vns[i]),
+                           stream, step_out)
+    # The graphs compute what the eager calls compute: step 0 both ways.
+    with torch.inference_mode(), torch.cuda.stream(stream):
+        graphs[0].replay()
+        got = step_out.clone()
+        want = [None] * LAYERS
+        run_steps(seq, decode, 1, outs=want)
+        want = torch.stack(want)
+    stream.synchronize()
     seq.rollback()
-    torch.cuda.synchronize()
+    if not torch.equal(got, want):
+        raise RuntimeError('step graph and eager step disagree')
 
-    # ---- device-timed region ------------------------------------------------
+    def replay_steps(first, k):
+        for s in range(first, first + k):
+            graphs[(s % cycle) % count].replay()
+
+    # untimed warm-up
+    with torch.cuda.stream(stream):
+        replay_steps(0, args.warmup)
+    stream.synchronize()
+
+    # ---- device-timed region: K steps, one graph replay each -------------------
     barrier(world)
     torch.cuda.synchronize()
     clocks.start()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push('timed')      # lets a profiler keep to the timed launches
-    start.record()
-    launches = run_steps(seq, decode, args.steps)
-    stop.record()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        replay_steps(0, args.steps)
+        stop.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     barrier(world)
     loop_ms = max_over_ranks(start.elapsed_time(stop), world)
+    launches = 2 * LAYERS * args.steps       # append + decode per layer per step
+    del graphs
+
+    # The same steps issued eagerly from Python (no graphs), for comparison.
+    seq.rollback()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eager_steps = min(args.steps, 4 * cycle)
+    start.record()
+    run_steps(seq, decode, eager_steps)
+    stop.record()
+    torch.cuda.synchronize()
+    eager_ms = max_over_ranks(start.elapsed_time(stop), world) / eager_steps
     seq.rollback()
 
     # ---- roofline of the decode kernel (the clock window extends over it) ----
@@ -462,7 +538,7 @@ def b200_arm(args, world, rank, local):
     ms = loop_ms / args.steps + amortised_ms          # per step
 
     # ---- end to end through the public API with host buffers -----------------
-    e2e = e2e_run(seq, args, world, device)
+    e2e = e2e_run(seq, args, world, device, decode, stream)
     e2e_ms = e2e['ms'] + amortised_ms
 
     value = world / (ms * 1e-3)
@@ -470,6 +546,10 @@ def b200_arm(args, world, rank, local):
             'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
             'us_per_step': ms * 1e3, 'us_per_layer': ms * 1e3 / LAYERS,
             'us_per_step_loop': loop_ms * 1e3 / args.steps,
+            'us_per_step_eager': eager_ms * 1e3,
+            'step_issue': 'one CUDA graph per step position of the cycle (append + decode per '
+                          'layer, outputs stacked), replayed once per step; us_per_step_eager '
+                          'issues the same calls from Python',
             'compaction_us_per_layer': compact_s * 1e6,
             'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'u8/bf16', 'data': 'synthetic (seeded N(0,1), 1% outlier channels x8)',
@@ -485,7 +565,9 @@ def b200_arm(args, world, rank, local):
             'clocks': clocks.summary(),
             'e2e': {'value': world / (e2e_ms * 1e-3), 'unit': 'tok/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
-                    'us_per_step': e2e_ms * 1e3},
+                    'us_per_step': e2e_ms * 1e3,
+                    'eager': {'value': world / ((e2e['eager_ms'] + amortised_ms) * 1e-3),
+                              'us_per_step': (e2e['eager_ms'] + amortised_ms) * 1e3}},
             'gpu_launches': launches}
     del seq
     torch.cuda.empty_cache()
@@ -502,46 +584,76 @@ def b200_arm(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def e2e_run(seq, args, world, device):
-    """The decode step through the public API (``compressed_kv_decode``), with
-    the step's query and new key/value rows copied from pinned host memory
-    and the 8 outputs read back to host memory every step; warmed up, then
-    ``args.steps`` steps timed (wall clock around a synchronised loop, max
-    over ranks)."""
-    from trpg_b200.compressed_kv_attention import compressed_kv_decode
+def e2e_run(seq, args, world, device, decode, stream):
+    """The decode step end to end: every step copies its query and new
+    key/value rows from pinned host memory into a device staging buffer
+    (one host-to-device copy), runs the 8 layers through the public API
+    (``append_for_attention`` + ``compressed_kv_decode``) and reads the 8
+    outputs back into host memory (one blocking device-to-host copy); warmed
+    up, then ``args.steps`` steps timed (wall clock around a synchronised
+    loop, max over ranks).
+
+    The layers run as the step's CUDA graph (captured from those API calls,
+    reading the staging buffer), the way a serving loop issues a decode
+    step; the same loop issuing the calls eagerly from Python is reported
+    beside it."""
     n = seq.q.shape[0]
     # One pinned buffer per step: q, k, v of all layers back to back.
     parts = (seq.q, seq.kn, seq.vn)
     flat = torch.cat([t.reshape(n, -1) for t in parts], 1).cpu().pin_memory()
     sizes = [t[0].numel() for t in parts]
     shapes = [t.shape[1:] for t in parts]
+    dev_in = torch.empty(flat.shape[1], dtype=flat.dtype, device=device)
+    q, kn, vn = (list(x.view(shape).unbind(0)) for x, shape in zip(dev_in.split(sizes), shapes))
     host_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
-    outs = [None] * LAYERS
+    dev_out = torch.empty(host_out.shape, dtype=host_out.dtype, device=device)
     cycle = ROLLBACK - 1
+    count = min(cycle, max(args.steps, args.warmup, 3))
+    graphs = capture_steps(seq, decode, count, lambda i: (q, kn, vn), stream, dev_out)
 
-    def steps(count):
-        for s in range(count):
-            i = s % cycle
-            if i == 0 and s:
-                seq.rollback()
-            dev = flat[i].to(device, non_blocking=True)
-            q, kn, vn = (x.view(shape).unbind(0) for x, shape in zip(dev.split(sizes), shapes))
-            with torch.inference_mode():
-                for li, layer in enumerate(seq.layers):
-                    view = layer.append_for_attention(kn[li], vn[li])
-                    outs[li] = compressed_kv_decode(q[li], view, SCALE)
-                    layer.compact_residual()
-                host_out.copy_(torch.stack(outs))   # blocking read of the step's result
+    def graph_steps(k):
+        with torch.cuda.stream(stream):
+            for s in range(k):
+                i = s % cycle
+                dev_in.copy_(flat[i], non_blocking=True)
+                graphs[i % count].replay()
+                host_out.copy_(dev_out)      # blocking read of the step's result
 
-    steps(max(3, args.warmup))
-    seq.rollback()
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    steps(args.steps)
-    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
-    seq.rollback()
-    return {'ms': e2e_ms / args.steps, 'h2d': flat[0].numel() * 2, 'd2h': host_out.numel() * 2}
+    outs = [None] * LAYERS
+
+    def eager_steps(k):
+        with torch.cuda.stream(stream):
+            for s in range(k):
+                i = s % cycle
+                if i == 0 and s:
+                    seq.rollback()
+                dev_in.copy_(flat[i], non_blocking=True)
+                with torch.inference_mode():
+                    for li, layer in enumerate(seq.layers):
+                        view = layer.append_for_attention(kn[li], vn[li])
+                        outs[li] = compressed_kv_decode(q[li], view, SCALE)
+                        layer.compact_residual()
+                    torch.stack(outs, out=dev_out)
+                host_out.copy_(dev_out)
+
+    from trpg_b200.compressed_kv_attention import compressed_kv_decode
+
+    def timed(fn, k):
+        fn(max(3, args.warmup))
+        seq.rollback()
+        barrier(world)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn(k)
+        ms = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+        seq.rollback()
+        return ms / k
+
+    graph_ms = timed(graph_steps, args.steps)
+    del graphs
+    eager_ms = timed(eager_steps, min(args.steps, 4 * cycle))
+    return {'ms': graph_ms, 'eager_ms': eager_ms, 'h2d': flat[0].numel() * 2,
+            'd2h': host_out.numel() * 2}
 
 
 # ---------------------------------------------------------------------------
