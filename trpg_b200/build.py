@@ -35,7 +35,7 @@ NVCC_FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-Xcompiler', '-fPIC', '--expt-r
               f'-I{INCLUDE}', f'-I{CSRC}']
 
 CU_SOURCES = ['ckv_capi.cu', 'ckv_pack.cu', 'ckv_attn.cu', 'ckv_static.cu', 'ckv_prefill.cu']
-HEADERS = ['ckv_common.cuh', 'ckv_attn.cuh']
+HEADERS = sorted(p.name for p in CSRC.glob('*.cuh'))
 
 
 def _run(cmd):
