@@ -270,10 +270,12 @@ def run_steps(seq, decode, steps, start=0, outs=None):
     return launches
 
 
-def capture_steps(seq, decode, count, inputs, stream, out):
+def capture_steps(seq, decode, count, inputs, stream, out, before=None, after=None):
     """One CUDA graph per step position i < count of the rollback cycle, each
     holding step i's 8 layers (append of the new key/value row into the
-    exact window, then decode) and the stack of the 8 outputs into `out`.
+    exact window, then decode) and the stack of the 8 outputs into `out`;
+    ``before(i)`` / ``after(i)`` add work captured ahead of / behind the
+    layers (the end-to-end loop's input and output copies).
 
     A serving loop replays the graph of the step it is at; the row a step
     appends and the length it attends over are fixed per position, so the
@@ -288,12 +290,16 @@ def capture_steps(seq, decode, count, inputs, stream, out):
             qs, kns, vns = inputs(i)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream, pool=pool):
+                if before is not None:
+                    before(i)
                 outs = []
                 for li, layer in enumerate(seq.layers):
                     view = layer.append_for_attention(kns[li], vns[li])
                     outs.append(decode(qs[li], view, SCALE))
                     layer.compact_residual()       # a no-op within the cycle
                 torch.stack(outs, out=out)
+                if after is not None:
+                    after(i)
             graphs.append(g)
     seq.rollback()
     return graphs
@@ -593,10 +599,12 @@ def e2e_run(seq, args, world, device, decode, stream):
     for); warmed up, then ``args.steps`` steps timed (wall clock around a
     synchronised loop, max over ranks).
 
-    The layers run as the step's CUDA graph (captured from those API calls,
-    reading the staging buffer), the way a serving loop issues a decode
-    step; the same loop issuing the calls eagerly from Python is reported
-    beside it."""
+    The step runs as its CUDA graph, captured from those API calls with the
+    two copies inside it (a memcpy node from step i's pinned input row at
+    the head, one into the pinned output buffer at the tail), the way a
+    serving loop replays a decode step; the host waits on an event recorded
+    after the replay.  The same loop issuing the copies and the API calls
+    eagerly from Python is reported beside it."""
     n = seq.q.shape[0]
     # One pinned buffer per step: q, k, v of all layers back to back.
     parts = (seq.q, seq.kn, seq.vn)
@@ -608,16 +616,16 @@ def e2e_run(seq, args, world, device, decode, stream):
     host_out = torch.empty(LAYERS, 1, HQ, 1, D, dtype=torch.bfloat16).pin_memory()
     dev_out = torch.empty(host_out.shape, dtype=host_out.dtype, device=device)
     cycle = ROLLBACK - 1
-    count = min(cycle, max(args.steps, args.warmup, 3))
-    graphs = capture_steps(seq, decode, count, lambda i: (q, kn, vn), stream, dev_out)
-
+    count = min(cycle, n, max(args.steps, args.warmup, 3))
     rows = [flat[i] for i in range(n)]          # the steps' pinned input rows, made once
+    graphs = capture_steps(seq, decode, count, lambda i: (q, kn, vn), stream, dev_out,
+                           before=lambda i: dev_in.copy_(rows[i], non_blocking=True),
+                           after=lambda i: host_out.copy_(dev_out, non_blocking=True))
     done = torch.cuda.Event()
 
-    def read_back():
-        # Asynchronous copy, then a spin on its event: the host resumes as
-        # soon as the copy lands instead of after a blocking wake-up.
-        host_out.copy_(dev_out, non_blocking=True)
+    def wait_done():
+        # Spin on the event: the host resumes as soon as the copy lands
+        # instead of after a blocking wake-up.
         done.record(stream)
         while not done.query():
             pass
@@ -625,10 +633,8 @@ def e2e_run(seq, args, world, device, decode, stream):
     def graph_steps(k):
         with torch.cuda.stream(stream):
             for s in range(k):
-                i = s % cycle
-                dev_in.copy_(rows[i], non_blocking=True)
-                graphs[i % count].replay()
-                read_back()
+                graphs[(s % cycle) % count].replay()
+                wait_done()
 
     outs = [None] * LAYERS
 
@@ -645,7 +651,8 @@ def e2e_run(seq, args, world, device, decode, stream):
                         outs[li] = compressed_kv_decode(q[li], view, SCALE)
                         layer.compact_residual()
                     torch.stack(outs, out=dev_out)
-                read_back()
+                host_out.copy_(dev_out, non_blocking=True)
+                wait_done()
 
     from trpg_b200.compressed_kv_attention import compressed_kv_decode
 

@@ -10,7 +10,6 @@
 #include <cudaTypedefs.h>
 
 #include "ckv_attn.cuh"
-#include "ckv_split.cuh"
 
 namespace ckv {
 namespace attn {
@@ -159,30 +158,21 @@ __global__ void __launch_bounds__(THREADS, 1) attn_kernel(const __grid_constant_
   }
   pdl_wait();
 
-  // Query B fragments (channel order of the MMA k index), filled by the QK
-  // warps while the producers start streaming: 16-bit pairs, or, for the
-  // folded rule, the four channels' values in fp32.
+  // Query B fragments (channel order of the MMA k index) as 16-bit pairs,
+  // filled by the QK warps while the producers start streaming.
   if (warp < QK_WARPS) {
     const T *qb = static_cast<const T *>(sd.q);
     for (int x = tid; x < C::KQS * NT * 32; x += QK_WARPS * 32) {
       const int ln = x & 31, nt = (x >> 5) % NT, s = (x >> 5) / NT;
       const int row = 8 * nt + (ln >> 2), cb = 16 * s + 2 * (ln & 3);
       const T *qrow = qb + (head * G + row % G) * sd.q_h + (row / G) * sd.q_n;
-      if constexpr (FOLD) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (row < rows)
-          v = make_float4(Elem<DT>::to_f32(qrow[cb]), Elem<DT>::to_f32(qrow[cb + 1]),
-                          Elem<DT>::to_f32(qrow[cb + 8]), Elem<DT>::to_f32(qrow[cb + 9]));
-        *reinterpret_cast<float4 *>(smem + C::OFF_Q + x * 16) = v;
-      } else {
-        uint2 v = make_uint2(0, 0);
-        if (row < rows) {
-          const uint16_t *qr = reinterpret_cast<const uint16_t *>(qrow);
-          v.x = qr[cb] | (uint32_t(qr[cb + 1]) << 16);
-          v.y = qr[cb + 8] | (uint32_t(qr[cb + 9]) << 16);
-        }
-        *reinterpret_cast<uint2 *>(smem + C::OFF_Q + x * 8) = v;
+      uint2 v = make_uint2(0, 0);
+      if (row < rows) {
+        const uint16_t *qr = reinterpret_cast<const uint16_t *>(qrow);
+        v.x = qr[cb] | (uint32_t(qr[cb + 1]) << 16);
+        v.y = qr[cb + 8] | (uint32_t(qr[cb + 9]) << 16);
       }
+      *reinterpret_cast<uint2 *>(smem + C::OFF_Q + x * 8) = v;
     }
     named_sync(BAR_QFRAG, QK_WARPS * 32);
   }
@@ -951,40 +941,17 @@ int launch(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st)
   return launch_kernel(attn_kernel<BITS, D, NT, DT, MAXS, FOLD>, C::SMEM, THREADS, pl, p, st, configured);
 }
 
-template <int D, int DT, int MAXS>
-int launch_split(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
-  static std::atomic<unsigned long long> configured[64];
-  Params<MAXS> &p = params_scratch<MAXS>();
-  const int fs = fill_params<8, D, MAXS>(a, pl, ws, p);
-  if (fs != CKV_OK) return fs;
-  return launch_kernel(split::split_kernel<D, DT, MAXS>, split::Cfg<D>::SMEM, split::THREADS, pl, p, st,
-                       configured);
-}
-
 template <int BITS, int D, int NT, int DT, bool FOLD>
 int dispatch_seqs(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
   return a.num_seqs == 1 ? launch<BITS, D, NT, DT, 1, FOLD>(a, pl, ws, st)
                          : launch<BITS, D, NT, DT, CKV_MAX_SEQS, FOLD>(a, pl, ws, st);
 }
 // The folded rule covers D = 128 and 256 (each value warp's channels fill
-// whole 16-byte chunks of the stage rows).  8-bit codes with up to 8 query
-// rows per KV head take the token-split kernel (ckv_split.cuh).
+// whole 16-byte chunks of the stage rows).
 template <int BITS, int D, int NT, int DT>
 int dispatch_fold(const ckv_attn_args &a, const Plan &pl, uint8_t *ws, cudaStream_t st) {
   if constexpr (D >= 128) {
-    if (a.flags & CKV_DEQUANT_FOLDED) {
-      if constexpr (BITS == 8 && NT == 1) {
-        // The split kernel reads each query row with 16-byte loads.
-        bool vec = true;
-        for (int i = 0; i < a.num_seqs; ++i)
-          vec = vec && al(a.seqs[i].query, 16) && a.seqs[i].q_stride_head % 8 == 0 &&
-                (a.nq == 1 || a.seqs[i].q_stride_pos % 8 == 0);
-        if (vec)
-          return a.num_seqs == 1 ? launch_split<D, DT, 1>(a, pl, ws, st)
-                                 : launch_split<D, DT, CKV_MAX_SEQS>(a, pl, ws, st);
-      }
-      return dispatch_seqs<BITS, D, NT, DT, true>(a, pl, ws, st);
-    }
+    if (a.flags & CKV_DEQUANT_FOLDED) return dispatch_seqs<BITS, D, NT, DT, true>(a, pl, ws, st);
   }
   return dispatch_seqs<BITS, D, NT, DT, false>(a, pl, ws, st);
 }

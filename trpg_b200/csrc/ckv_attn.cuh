@@ -132,7 +132,7 @@ struct Cfg {
   static constexpr int VCODE = 128 * VROWB;
   static constexpr int VMETA = 128 * NG * 8;
   static constexpr int VST = align1k(cmax(VCODE + VMETA, RBYTES));
-  static constexpr int NV = (NT == 1 && !FOLD) ? 3 : 2; // V stage ring depth
+  static constexpr int NV = NT == 1 ? 3 : 2;            // V stage ring depth
   // QK: each warp covers all D channels in KQS k-steps of 16.
   static constexpr int KQS = D / 16;
   // PV: each warp covers D/4 channels, CPL per lane, MTV m-tiles.
@@ -141,9 +141,8 @@ struct Cfg {
   // Shared-memory map (offsets from a 1024-byte aligned base).
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + NK * KST;
-  // Query fragments per (k-step, n-tile, lane): two 16-bit pairs (8 bytes,
-  // exact rule) or the four channels' fp32 values (16 bytes, folded rule).
-  static constexpr int QFRAG = FOLD ? 16 : 8;
+  // Query fragments per (k-step, n-tile, lane): two 16-bit pairs (8 bytes).
+  static constexpr int QFRAG = 8;
   static constexpr int OFF_Q = OFF_V + NV * VST;                   // [KQS][NT][32] query fragments
   static constexpr int OFF_P = OFF_Q + KQS * NT * 32 * QFRAG;      // [TEAMS][2][ROWS][PP]
   static constexpr int OFF_XM = OFF_P + TEAMS * 2 * ROWS * PP;     // [TEAMS][2][4][ROWS] P scales m_q
@@ -280,12 +279,7 @@ struct QkWarp {
   // B fragment of the query (16-bit pairs): channels 16s + 2qd, +1 and
   // 16s + 2qd + 8, +9 of query row 8nt + r.
   __device__ __forceinline__ uint2 qfrag(int s, int nt) const {
-    if constexpr (FOLD) {
-      const float4 v = lds<float4>(qfr, ((s * NT + nt) * 32 + lane) * 16);
-      return make_uint2(E::pack2(v.x, v.y), E::pack2(v.z, v.w));
-    } else {
-      return lds<uint2>(qfr, ((s * NT + nt) * 32 + lane) * 8);
-    }
+    return lds<uint2>(qfr, ((s * NT + nt) * 32 + lane) * 8);
   }
 
   // Token (within the item) of logit S[mt][nt][2u + j] of a packed block.
@@ -340,13 +334,15 @@ struct QkWarp {
       uint32_t b[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const float4 qv = lds<float4>(qfr, ((s * NT + nt) * 32 + lane) * 16);
-        const float2 w01 = __fmul2_rn(make_float2(qv.x, qv.y), make_float2(m0.x, m0.z));
-        const float2 w89 = __fmul2_rn(make_float2(qv.z, qv.w), make_float2(m1.x, m1.z));
+        // The query as stored (16-bit pairs), widened exactly to fp32.
+        const uint2 qp = qfrag(s, nt);
+        const float2 q01 = E::unpack2(qp.x), q89 = E::unpack2(qp.y);
+        const float2 w01 = __fmul2_rn(q01, make_float2(m0.x, m0.z));
+        const float2 w89 = __fmul2_rn(q89, make_float2(m1.x, m1.z));
         b[nt][0] = f16x2_sat(w01.x, w01.y);
         b[nt][1] = f16x2_sat(w89.x, w89.y);
-        clow[nt] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(m0.y, m0.w), clow[nt]);
-        clow[nt] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(m1.y, m1.w), clow[nt]);
+        clow[nt] = __ffma2_rn(q01, make_float2(m0.y, m0.w), clow[nt]);
+        clow[nt] = __ffma2_rn(q89, make_float2(m1.y, m1.w), clow[nt]);
         mma16816<CKV_F16>(corr[nt], one, b[nt][0], b[nt][1]);
       }
       uint32_t a[2][4];
