@@ -723,9 +723,11 @@ def view_bytes_q(view, nq=1) -> int:
     return HKV * (view.packed_tokens * per_token + view.keys.shape[2] * 2 * D * 2) + 2 * HQ * nq * D * 2
 
 
-def graph_seconds(fn, replays=20):
+def graph_seconds(fn, replays=20, align=None):
     """Device seconds per call of `fn`, from a CUDA graph of one call replayed
-    back to back between events on the capturing stream."""
+    back to back between events on the capturing stream.  ``align`` runs
+    before the timed replays (a barrier, when the call waits for other
+    ranks, so that no rank's time counts another rank's late start)."""
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.inference_mode():
@@ -739,6 +741,10 @@ def graph_seconds(fn, replays=20):
         with torch.cuda.stream(stream):
             for _ in range(3):
                 graph.replay()
+        if align is not None:
+            stream.synchronize()
+            align()
+        with torch.cuda.stream(stream):
             a.record(stream)
             for _ in range(replays):
                 graph.replay()
@@ -855,6 +861,26 @@ def measure_extra(w, args, world, rank, device, min_steps=20):
         combine_us = statistics.median(e[1].elapsed_time(e[2]) for e in ev) * 1e3
         out['us_partial_max_rank'] = max_over_ranks(compute, world)
         out['us_allgather_combine_max_rank'] = max_over_ranks(combine_us, world)
+        # The same exchange over NVLink peer mappings instead of NCCL: one
+        # launch per rank publishes its partial into every rank's buffer and
+        # merges once all have arrived.  Timed as CUDA-graph replays of the
+        # step (partial + exchange) and of the exchange alone.
+        from trpg_b200.sharding import PeerExchange
+        with torch.inference_mode():
+            part0 = fn()[0]
+        px = PeerExchange(part0.shape[0], D)
+        try:
+            align = lambda: (barrier(world), torch.cuda.synchronize())
+            step_s = graph_seconds(lambda: px.combine(fn()[0], torch.bfloat16), replays=200, align=align)
+            ex_s = graph_seconds(lambda: px.combine(part0, torch.bfloat16), replays=200, align=align)
+            failed = px.error()
+        finally:
+            px.close()
+        step_us = max_over_ranks(step_s * 1e6, world)
+        out['peer_exchange'] = {'us_per_step_max_rank': step_us,
+                                'us_exchange_combine_max_rank': max_over_ranks(ex_s * 1e6, world),
+                                'value': tokens / (step_us * 1e-6), 'unit': 'tok/s',
+                                'wait_gave_up': bool(max_over_ranks(float(failed), world))}
     return out
 
 

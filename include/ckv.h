@@ -288,6 +288,56 @@ int ckv_prefill_workspace(const ckv_prefill_args *args, size_t *bytes);
 int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t workspace_bytes,
                 ckv_stream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Split-KV partials exchanged over peer memory (one process per GPU)     */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * The cross-GPU half of sequence-split-KV decode without a collective
+ * library: every rank owns one exchange buffer, maps every other rank's
+ * buffer into its address space (CUDA IPC over NVLink, plain peer mappings,
+ * no multicast), and one launch per rank and step
+ *   1. writes this rank's partial (rows x (D+2) fp32, as ckv_attention with
+ *      partial = 1 leaves it) into every rank's buffer, then raises this
+ *      rank's flag in every buffer (system-scope release);
+ *   2. waits until the flags of all ranks are raised in its own buffer
+ *      (system-scope acquire; bounded: after `spin_limit` clock cycles, or
+ *      2^31 when 0, it sets the buffer's error word and skips step 3);
+ *   3. merges the world partials into `out` [rows, D] of `dtype`, with the
+ *      rule of ckv_combine_partials (models/compressed_kv_kernels.py:85-89).
+ * The step number is a counter in the buffer that each launch advances, so
+ * the launch can be captured in a CUDA graph and replayed. Partials and
+ * flags alternate between two slots by step parity: a rank's step s + 1
+ * waits for every rank's step s + 1 partial, which each rank publishes only
+ * after its own step s, so no rank overwrites a slot that another rank is
+ * still reading. Every rank must make the same sequence of calls.
+ *
+ * Buffer: ckv_exchange_bytes(world, rows, head_dim) bytes, zeroed, from
+ * ckv_exchange_alloc; world <= CKV_EXCHANGE_MAX_WORLD.
+ */
+#define CKV_EXCHANGE_MAX_WORLD 8
+size_t ckv_exchange_bytes(int world, int64_t rows, int head_dim);
+/* cudaMalloc + clear of one exchange buffer on the current device, and its
+ * CUDA IPC handle (64 bytes) for the other ranks. */
+int ckv_exchange_alloc(int world, int64_t rows, int head_dim, void **buffer,
+                       unsigned char handle[64]);
+/* Map another rank's buffer (from its handle) into this process. */
+int ckv_exchange_open(const unsigned char handle[64], void **peer_buffer);
+/* Unmap a buffer from ckv_exchange_open / free one from ckv_exchange_alloc.
+ * No launch that uses it may still be in flight on any rank. */
+int ckv_exchange_close(void *peer_buffer);
+int ckv_exchange_free(void *buffer);
+/* buffers[r]: rank r's buffer as seen by this process (buffers[rank] is this
+ * rank's own).  phases: 3 for both phases in one launch (one rank per GPU);
+ * 1 (publish only) and 2 (wait and merge only) let one process drive several
+ * ranks' buffers on one GPU without launches that wait on each other. */
+int ckv_exchange_combine(const float *partial, int64_t rows, int head_dim, void *const *buffers,
+                         int world, int rank, int phases, long long spin_limit, int dtype,
+                         void *out, ckv_stream_t stream);
+/* The buffer's error word (1 after a wait gave up), read and cleared on
+ * `stream` (synchronises the stream). */
+int ckv_exchange_error(void *buffer, int *flag, ckv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,3 +65,22 @@ def test_cpu_tensors_raise_instead_of_falling_back():
     from trpg_b200 import quantized_kv_kernels as Q
     with pytest.raises(RuntimeError):
         Q.pack(torch.zeros(4, 64, dtype=torch.bfloat16), 8)
+
+
+def test_exchange_sizes_and_arguments_are_checked_on_the_host():
+    lib = _native.library()
+    rows, d = 16, 256
+    want = 512 + 2 * 2 * rows * (d + 2) * 4
+    assert lib.ckv_exchange_bytes(2, rows, d) == (want + 255) // 256 * 256
+    assert lib.ckv_exchange_bytes(0, rows, d) == 0
+    assert lib.ckv_exchange_bytes(9, rows, d) == 0           # above CKV_EXCHANGE_MAX_WORLD
+    assert lib.ckv_exchange_bytes(2, rows, 255) == 0         # odd head_dim
+    lib.ckv_exchange_combine.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                                         ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p,
+                                         ctypes.c_void_p]
+    assert lib.ckv_exchange_combine(None, rows, d, None, 2, 0, 3, 0, 0, None, None) == 1
+    bufs = (ctypes.c_void_p * 2)(256, 512)
+    assert lib.ckv_exchange_combine(None, rows, d, bufs, 2, 2, 3, 0, 0, None, None) == 1  # rank
+    assert lib.ckv_exchange_combine(None, rows, d, bufs, 2, 0, 4, 0, 0, None, None) == 1  # phases
+    assert lib.ckv_exchange_combine(None, rows, d, bufs, 2, 0, 1, 0, 0, None, None) == 1  # no partial

@@ -21,7 +21,9 @@ TORCH_LIB_PATH = PKG / '_ckv_torch.so'
 EXPORTS = ('ckv_status_string', 'ckv_last_error', 'ckv_version', 'ckv_pack_rows',
            'ckv_unpack_rows', 'ckv_pack_append', 'ckv_residual_append', 'ckv_attention_workspace',
            'ckv_attention_error', 'ckv_attention', 'ckv_attention_static',
-           'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill')
+           'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill', 'ckv_exchange_bytes',
+           'ckv_exchange_alloc', 'ckv_exchange_open', 'ckv_exchange_close', 'ckv_exchange_free',
+           'ckv_exchange_combine', 'ckv_exchange_error')
 
 ROUNDING = {'half_even': 0, 'half_up': 1}
 DEQUANT_MODES = ('exact', 'folded')
@@ -40,6 +42,14 @@ def library() -> ctypes.CDLL:
         _lib = ctypes.CDLL(str(LIB_PATH))
         _lib.ckv_status_string.restype = ctypes.c_char_p
         _lib.ckv_last_error.restype = ctypes.c_char_p
+        _lib.ckv_exchange_bytes.restype = ctypes.c_size_t
+        _lib.ckv_exchange_bytes.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_int]
+        _lib.ckv_exchange_alloc.argtypes = [ctypes.c_int, ctypes.c_int64, ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
+        _lib.ckv_exchange_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        _lib.ckv_exchange_close.argtypes = [ctypes.c_void_p]
+        _lib.ckv_exchange_free.argtypes = [ctypes.c_void_p]
+        _lib.ckv_exchange_error.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
     return _lib
 
 

@@ -34,7 +34,8 @@ ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 NVCC_FLAGS = ['-O3', '-std=c++17', '-lineinfo', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr',
               f'-I{INCLUDE}', f'-I{CSRC}']
 
-CU_SOURCES = ['ckv_capi.cu', 'ckv_pack.cu', 'ckv_attn.cu', 'ckv_static.cu', 'ckv_prefill.cu']
+CU_SOURCES = ['ckv_capi.cu', 'ckv_pack.cu', 'ckv_attn.cu', 'ckv_static.cu', 'ckv_prefill.cu',
+              'ckv_exchange.cu']
 HEADERS = sorted(p.name for p in CSRC.glob('*.cuh'))
 
 

@@ -600,6 +600,28 @@ Tensor combine_partials(const Tensor &partials, at::ScalarType dtype) {
   return out;
 }
 
+// One rank's step of the peer exchange (ckv_exchange_combine): partial
+// [rows, D+2] fp32 published to every rank's buffer, then the merged
+// [rows, D] output (left unwritten when phases is 1, publish only).
+Tensor exchange_combine(const Tensor &partial, std::vector<int64_t> buffers, int64_t rank,
+                        int64_t phases, int64_t spin_limit, at::ScalarType dtype) {
+  require_cuda(partial, "partial");
+  TORCH_CHECK(partial.dim() == 2 && partial.scalar_type() == at::kFloat && partial.is_contiguous(),
+              "ckv::exchange_combine: partial must be contiguous float32 [rows, D+2]");
+  TORCH_CHECK(!buffers.empty() && buffers.size() <= CKV_EXCHANGE_MAX_WORLD,
+              "ckv::exchange_combine: 1..", CKV_EXCHANGE_MAX_WORLD, " buffers");
+  c10::cuda::CUDAGuard guard(partial.device());
+  const int64_t rows = partial.size(0), D = partial.size(1) - 2;
+  Tensor out = at::empty({rows, D}, partial.options().dtype(dtype));
+  void *bufs[CKV_EXCHANGE_MAX_WORLD];
+  for (size_t i = 0; i < buffers.size(); ++i) bufs[i] = reinterpret_cast<void *>(buffers[i]);
+  check_status(ckv_exchange_combine(partial.data_ptr<float>(), rows, int(D), bufs, int(buffers.size()),
+                                    int(rank), int(phases), spin_limit, dtype_code(dtype),
+                                    out.data_ptr(), current_stream(partial)),
+               "exchange_combine");
+  return out;
+}
+
 // Error word of every cached attention workspace on `like`'s device (1 when
 // a kernel gave up waiting for a copy or a peer warp and aborted, so that
 // call's outputs are not valid).  Reading waits for each stream; the words
@@ -662,6 +684,8 @@ TORCH_LIBRARY(ckv, m) {
   m.def("window_append(Tensor keys_new, Tensor values_new, Tensor(a!) keys, Tensor(b!) values, "
         "int capacity) -> (Tensor(a), Tensor(b))");
   m.def("set_dequant(int mode) -> int", &set_dequant);
+  m.def("exchange_combine(Tensor partial, int[] buffers, int rank, int phases, int spin_limit, "
+        "ScalarType dtype) -> Tensor");
 }
 
 namespace {
@@ -695,6 +719,7 @@ TORCH_LIBRARY_IMPL(ckv, CUDA, m) {
   m.impl("pack_append", &pack_append);
   m.impl("attention", &attention_opt);
   m.impl("combine_partials", &combine_partials);
+  m.impl("exchange_combine", &exchange_combine);
   m.impl("decode", &decode);
   m.impl("attention_error", &attention_error);
   m.impl("residual_append", &residual_append);

@@ -7,8 +7,12 @@ Two strategies, one process per GPU (``torch.distributed``):
 * sequence-split-KV -- one long sequence's packed 128-token blocks are split
   into contiguous ranges, one per rank; the last rank also owns the exact
   residual window.  Each rank produces (m, l, o) partials with the same
-  kernel (``partial=True``), the partials are all-gathered over NCCL, and the
-  log-sum-exp rule of ``models/compressed_kv_kernels.py:85-89`` merges them.
+  kernel (``partial=True``); the log-sum-exp rule of
+  ``models/compressed_kv_kernels.py:85-89`` merges them.  The partials cross
+  GPUs either through ``PeerExchange`` (one launch per rank writes its
+  partial into every rank's buffer over NVLink peer mappings and merges once
+  all have arrived, no collective library) or through an NCCL all-gather
+  followed by the merge kernel (``gather_partials``).
 
 The reference is single-GPU (``models/compressed_kv_attention.py:10``); both
 strategies are new.
@@ -85,18 +89,96 @@ def gather_partials(partial: torch.Tensor, group=None) -> torch.Tensor:
     return out.view(world, *partial.shape)
 
 
-def split_kv_attention(query: torch.Tensor, view, scale: float, group=None) -> torch.Tensor:
+class PeerExchange:
+    """Exchange of split-KV partials over peer memory between the ranks of a
+    process group (one process per GPU), the ``ckv_exchange_*`` calls of
+    ``include/ckv.h``.
+
+    Each rank allocates one buffer, the ranks swap its CUDA IPC handle
+    (``all_gather_object`` on ``group``, once), and every rank maps the
+    others' buffers.  ``combine(partial)`` is then one launch per rank and
+    step: publish this rank's partial into every buffer, wait for all ranks'
+    partials of the step (bounded), merge.  It never synchronises the host,
+    keeps its step count on the device (so it can be captured in a CUDA
+    graph), and every rank must call it the same number of times.
+    ``close()`` waits for the device and for the other ranks before it
+    unmaps and frees.
+    """
+
+    def __init__(self, rows: int, head_dim: int, group=None, spin_limit: int = 0):
+        import ctypes
+        import torch.distributed as dist
+        from . import _native
+        self.group = group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.rows, self.head_dim, self.spin_limit = rows, head_dim, spin_limit
+        lib = self._lib = _native.library()
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _check(lib, lib.ckv_exchange_alloc(self.world, rows, head_dim, ctypes.byref(own), handle))
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._peers = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            _check(lib, lib.ckv_exchange_open(h, ctypes.byref(peer)))
+            self._peers.append(peer.value)
+            ptrs.append(peer.value)
+        self.buffers = ptrs
+
+    def combine(self, partial: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """This rank's partial [rows, D+2] fp32 in, the merged [rows, D] out."""
+        from ._native import ops
+        return ops().exchange_combine(partial, self.buffers, self.rank, 3, self.spin_limit, dtype)
+
+    def error(self) -> int:
+        """1 if a wait of this rank's launches gave up since the last check."""
+        import ctypes
+        flag = ctypes.c_int(0)
+        stream = torch.cuda.current_stream().cuda_stream
+        _check(self._lib, self._lib.ckv_exchange_error(self._own, ctypes.byref(flag), stream))
+        return flag.value
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)        # no rank still writes into a buffer
+        for p in self._peers:
+            _check(self._lib, self._lib.ckv_exchange_close(p))
+        dist.barrier(group=self.group)        # no rank still maps this one
+        _check(self._lib, self._lib.ckv_exchange_free(self._own))
+        self._own, self._peers, self.buffers = None, [], []
+
+
+def _check(lib, status: int) -> None:
+    if status != 0:
+        raise RuntimeError(f'ckv: {lib.ckv_status_string(status).decode()}: '
+                           f'{lib.ckv_last_error().decode()}')
+
+
+def split_kv_attention(query: torch.Tensor, view, scale: float, group=None,
+                       exchange: PeerExchange | None = None) -> torch.Tensor:
     """Attention of one sequence split across the ranks of ``group``.
 
     Every rank passes the same query and a view of the same cache (each rank
     only reads its own block range and, on the last rank, the residual).
-    Returns the full output on every rank.
+    Returns the full output on every rank.  With ``exchange`` the partials
+    cross GPUs through peer memory; without it, through an NCCL all-gather.
     """
     import torch.distributed as dist
     from . import compressed_kv_kernels as K
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     rng = split_kv_range(view.packed_tokens // 128, view.keys.shape[2], world, rank)
     part = K.attention([query], [view], scale, ranges=[rng], partial=True)[0]
-    parts = gather_partials(part, group)
-    out = K.combine(parts, query.dtype)
+    if exchange is not None:
+        out = exchange.combine(part, query.dtype)
+    else:
+        out = K.combine(gather_partials(part, group), query.dtype)
     return out.view(query.shape)
