@@ -287,6 +287,14 @@ int ckv_prefill_workspace(const ckv_prefill_args *args, size_t *bytes);
  * when that is 0). */
 int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t workspace_bytes,
                 ckv_stream_t stream);
+/* 1 if a ckv_prefill launch on the current device gave up a bounded wait on
+ * its tensor-core products since the last call (its outputs are then not
+ * valid); read and cleared on `stream`, which it synchronises. */
+int ckv_prefill_error(int *flag, ckv_stream_t stream);
+/* Selects the prefill kernel for head_dim 128 / 256 (process-wide): 1 the
+ * tcgen05 kernel (operands in shared memory, accumulators in tensor memory),
+ * 0 the mma.sync kernel.  Same results up to fp32 summation order. */
+int ckv_prefill_set_tensor_cores(int on);
 
 /* ---------------------------------------------------------------------- */
 /* Split-KV partials exchanged over peer memory (one process per GPU)     */

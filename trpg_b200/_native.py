@@ -21,7 +21,8 @@ TORCH_LIB_PATH = PKG / '_ckv_torch.so'
 EXPORTS = ('ckv_status_string', 'ckv_last_error', 'ckv_version', 'ckv_pack_rows',
            'ckv_unpack_rows', 'ckv_pack_append', 'ckv_residual_append', 'ckv_attention_workspace',
            'ckv_attention_error', 'ckv_attention', 'ckv_attention_static',
-           'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill', 'ckv_exchange_bytes',
+           'ckv_combine_partials', 'ckv_prefill_workspace', 'ckv_prefill', 'ckv_prefill_error',
+           'ckv_prefill_set_tensor_cores', 'ckv_exchange_bytes',
            'ckv_exchange_alloc', 'ckv_exchange_open', 'ckv_exchange_close', 'ckv_exchange_free',
            'ckv_exchange_combine', 'ckv_exchange_error')
 

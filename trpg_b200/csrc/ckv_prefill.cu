@@ -455,6 +455,401 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
   }
 }
 
+// ---------------------------------------------------------------------------
+// 5th-generation tensor-core variant (tcgen05, D = 128 / 256).
+//
+// Same work split, dequantization, softmax rule, masks and partial records
+// as prefill_kernel; the two products run on tcgen05.mma with both operands
+// in shared memory and the fp32 accumulators in tensor memory:
+//   S = Q K^T   M = 128 query rows, N = 64 tokens, K = D     -> TMEM columns [0, 64)
+//   O += P V    M = 128 query rows, N = D,         K = 64    -> TMEM columns [256, 256 + D)
+// Shared-memory tiles, 16-bit, in the canonical 128-byte-swizzled layouts
+// (16-byte chunk c of a 128-byte row r stored at chunk c ^ (r & 7); 1024-byte
+// atoms of 8 rows):
+//   Q   K-major:  [D/64 blocks][128 rows][64 channels]
+//   K   packed:   MN-major [D channel rows][64 tokens] (the bank's channel-major
+//                 order, so dequantized codes are stored without a transpose);
+//       window:   K-major  [D/64 blocks][64 token rows][64 channels] (the
+//                 window's token-major order)
+//   V   MN-major: [D/64 blocks][64 token rows][64 channels]
+//   P   K-major:  [128 rows][64 tokens]
+// One thread issues the MMAs; tcgen05.commit signals an mbarrier when they
+// complete.  Warps 0-3 own the 128 accumulator lanes (thread = query row):
+// each loads its row of S from tensor memory, runs the online softmax, writes
+// its P row, and rescales its O row in tensor memory when its maximum grows.
+// All eight warps dequantize; the next packed tile's codes are read into
+// registers while this tile's products run.
+namespace tc {
+
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;
+
+template <int D>
+struct TCfg {
+  static constexpr int BT = 64;
+  static constexpr int Q_BYTES = BM * D * 2;           // 128 rows
+  static constexpr int KV_BYTES = D * BT * 2;          // one K or V tile
+  static constexpr int P_BYTES = BM * BT * 2;
+  static constexpr int OFF_Q = 0, OFF_K = Q_BYTES, OFF_V = OFF_K + KV_BYTES, OFF_P = OFF_V + KV_BYTES;
+  static constexpr int SMEM = OFF_P + P_BYTES + 1024;  // + alignment slack
+  static_assert(D % 64 == 0 && D <= 256, "head_dim");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// Shared-memory matrix descriptor: start, leading / stride byte offsets
+// (16-byte units), the sm_100 descriptor version (1), 128-byte swizzle (2).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor of kind::f16: fp32 accumulator, A and B of the query
+// dtype, their major-ness (0 = K-major, 1 = MN-major), N and M.
+template <int DT>
+constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
+  constexpr uint32_t fmt = DT == CKV_BF16 ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes become visible to the tensor cores.
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 32 consecutive fp32 columns of this thread's lane (32x32b shape; the whole
+// warp must execute it).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of 128-byte row `r` in a swizzled tile.
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ unsigned g_error;   // set when a bounded wait gave up (ckv_prefill_error)
+
+__device__ __forceinline__ void wait_bar(uint32_t bar, uint32_t parity) {
+  if (!mbar_wait(bar, parity)) atomicOr(&g_error, 1u);
+}
+
+// A packed tile's codes (registers, read_packed's split) into K (MN-major,
+// channel rows) and V (MN-major, token rows) in the swizzled layouts.
+template <int BITS, int D, int DT>
+__device__ __forceinline__ void write_packed_tc(const PackedRegs<BITS, D> &r, uint32_t ks,
+                                                uint32_t vs, int tid) {
+  using C = Cfg<D>;
+  constexpr int SB = C::BT / 16;
+#pragma unroll
+  for (int j = 0; j < C::K_TASKS; ++j) {
+    const int i = tid + j * kThreads, d = i / SB, c = (i % SB) * 2;   // chunks c, c + 1 of row d
+    uint4 lo, hi;
+    dequant16<BITS, DT>(r.k[j], r.km[j].x, r.km[j].y, lo, hi);
+    sts128(ks + swz128(d, c), lo);
+    sts128(ks + swz128(d, c + 1), hi);
+  }
+  constexpr int CH = D / 16;
+#pragma unroll
+  for (int j = 0; j < C::V_TASKS; ++j) {
+    const int i = tid + j * kThreads, t = i / CH, c0 = (i % CH) * 16;
+    uint4 lo, hi;
+    dequant16<BITS, DT>(r.v[j], r.vm[j].x, r.vm[j].y, lo, hi);
+    const uint32_t blk = vs + uint32_t(c0 >> 6) * (64 * 128);
+    const int c = (c0 & 63) >> 3;
+    sts128(blk + swz128(t, c), lo);
+    sts128(blk + swz128(t, c + 1), hi);
+  }
+}
+
+// Window tile: rows [t0, t0 + 64) of the exact K and V, zero past R, into K
+// (K-major, token rows) and V (MN-major, token rows).
+template <int D>
+__device__ __forceinline__ void write_resid_tc(const Params &p, int kvh, int t0, int tid, uint32_t ks,
+                                               uint32_t vs) {
+  constexpr int CH = D / 8;   // 16-byte chunks of a row
+  const uint16_t *rk = static_cast<const uint16_t *>(p.rk) + kvh * p.rks_h;
+  const uint16_t *rv = static_cast<const uint16_t *>(p.rv) + kvh * p.rvs_h;
+  for (int i = tid; i < 64 * CH; i += kThreads) {
+    const int t = i / CH, c8 = i % CH, tt = t0 + t;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+    if (tt < p.resid) {
+      kv = __ldg(reinterpret_cast<const uint4 *>(rk + int64_t(tt) * p.rks_t + c8 * 8));
+      vv = __ldg(reinterpret_cast<const uint4 *>(rv + int64_t(tt) * p.rvs_t + c8 * 8));
+    }
+    const uint32_t blk = uint32_t(c8 >> 3) * (64 * 128);
+    sts128(ks + blk + swz128(t, c8 & 7), kv);
+    sts128(vs + blk + swz128(t, c8 & 7), vv);
+  }
+}
+
+template <int BITS, int D, int DT>
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ Params p) {
+  using T = TCfg<D>;
+  using E = Elem<DT>;
+  constexpr int BT = T::BT;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t s_bar[2];   // S products done, O products done
+  __shared__ uint32_t s_tmem;
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t qs = sb + T::OFF_Q, ks = sb + T::OFF_K, vs = sb + T::OFF_V, ps = sb + T::OFF_P;
+  const uint32_t bar_s = smem_u32(&s_bar[0]), bar_o = smem_u32(&s_bar[1]);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int kvh = blockIdx.y;
+  const int tile = gridDim.x - 1 - blockIdx.x;
+  const int G = p.groups, nrows = p.qlen * G, r0 = tile * BM;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    mbar_fence_init();
+  }
+  // Query tile, K-major: row r, channels 64b + 8c.. at block b, chunk c.
+  {
+    constexpr int CH = D / 8;
+    const uint16_t *q = static_cast<const uint16_t *>(p.q);
+    for (int i = tid; i < BM * CH; i += kThreads) {
+      const int r = i / CH, c8 = i % CH, gr = r0 + r;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (gr < nrows) {
+        const int pos = gr / G, h = kvh * G + gr % G;
+        v = __ldg(reinterpret_cast<const uint4 *>(q + h * p.qhs + int64_t(pos) * p.qts + c8 * 8));
+      }
+      sts128(qs + uint32_t(c8 >> 3) * (BM * 128) + swz128(r, c8 & 7), v);
+    }
+  }
+  fence_async_smem();
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = s_tmem;
+
+  // Items of this CTA's history split, as in prefill_kernel.
+  const int z = p.splits - 1 - int(blockIdx.z), ntiles = p.packed / BT;
+  const int last_row = min(r0 + BM, nrows) - 1;
+  const int rstop = min(p.resid, p.resid - p.qlen + last_row / G + 1);
+  const int total = ntiles + (rstop + BT - 1) / BT;
+  const int a0 = int(int64_t(total) * z / p.splits), a1 = int(int64_t(total) * (z + 1) / p.splits);
+  const int i0 = min(a0, ntiles), np = min(a1, ntiles) - i0;
+  const int rb = max(a0, ntiles) - ntiles, nr = max(a1, ntiles) - ntiles - rb;
+
+  // Row state (warps 0-3: thread tid owns query row tid of the tile).
+  const bool row_owner = warp < 4;
+  const int gr = r0 + tid;
+  const int vis = p.resid - p.qlen + (row_owner ? gr : 0) / G;
+  float m = -INFINITY, l = 0.f;
+  const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+
+  constexpr uint32_t ID_S_PACKED = idesc<DT>(BM, BT, 0, 1);
+  constexpr uint32_t ID_S_RESID = idesc<DT>(BM, BT, 0, 0);
+  constexpr uint32_t ID_O = idesc<DT>(BM, D, 0, 1);
+
+  PackedRegs<BITS, D> pr;
+  if (np > 0) read_packed<BITS, D>(p, kvh, i0 * BT, tid, pr);
+  const int n_items = np + nr;
+  bool o_live = false;   // O holds a product (the first one overwrites)
+  for (int it = 0; it < n_items; ++it) {
+    const bool packed = it < np;
+    const int tbase = packed ? 0 : (rb + it - np) * BT;
+    // ---- this tile into shared memory ------------------------------------------
+    if (packed) {
+      write_packed_tc<BITS, D, DT>(pr, ks, vs, tid);
+      if (it + 1 < np) read_packed<BITS, D>(p, kvh, (i0 + it + 1) * BT, tid, pr);
+    } else {
+      write_resid_tc<D>(p, kvh, tbase, tid, ks, vs);
+    }
+    fence_async_smem();
+    __syncthreads();
+    // ---- S = Q K^T -----------------------------------------------------------------
+    if (tid == 0) {
+      fence_after();
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint64_t da = sdesc(qs + uint32_t(kk >> 2) * (BM * 128) + uint32_t(kk & 3) * 32, 16, 1024);
+        uint64_t db;
+        if (packed)   // MN-major: channel rows 16kk.. (two 8-row groups)
+          db = sdesc(ks + uint32_t(kk) * 2048, T::KV_BYTES, 1024);
+        else          // K-major: token rows, channels 16kk.. in block kk / 4
+          db = sdesc(ks + uint32_t(kk >> 2) * (64 * 128) + uint32_t(kk & 3) * 32, 16, 1024);
+        umma(tmem, da, db, packed ? ID_S_PACKED : ID_S_RESID, kk > 0);
+      }
+      umma_commit(bar_s);
+    }
+    // ---- online softmax of the tile's S rows, P into shared memory -------------------
+    if (row_owner) {
+      wait_bar(bar_s, uint32_t(it & 1));
+      __syncwarp();   // the tensor-memory loads are warp-collective
+      fence_after();
+      float s[BT];
+      {
+        float h[32];
+        tmem_ld32(tmem + lane_base + 0, h);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s[j] = h[j];
+        tmem_ld32(tmem + lane_base + 32, h);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s[32 + j] = h[j];
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < BT; ++j) {
+        float x = s[j] * p.scale_log2;
+        if (!packed) {
+          const int t = tbase + j;
+          if (t >= p.resid || t > vis) x = -INFINITY;
+        }
+        s[j] = x;
+        mx = fmaxf(mx, x);
+      }
+      float nm = fmaxf(m, mx);
+      if (nm == -INFINITY) nm = 0.f;   // nothing visible yet: no inf - inf
+      const float alpha = ex2(m - nm);
+      m = nm;
+      if (__any_sync(0xffffffffu, o_live && alpha != 1.f)) {
+        // Rescale the warp's O rows (the previous tile's products are
+        // complete); rows that kept their maximum multiply by 1.
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(tmem + lane_base + kOCol + c, o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] *= alpha;
+          tmem_st32(tmem + lane_base + kOCol + c, o);
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BT / 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float e0 = ex2(s[8 * c + 2 * k] - m), e1 = ex2(s[8 * c + 2 * k + 1] - m);
+          rs += e0 + e1;
+          w[k] = E::pack2(e0, e1);
+        }
+        sts128(ps + swz128(tid, c), make_uint4(w[0], w[1], w[2], w[3]));
+      }
+      l = l * alpha + rs;
+      fence_async_smem();
+      fence_before();
+    }
+    __syncthreads();
+    // ---- O += P V ------------------------------------------------------------------
+    if (tid == 0) {
+      fence_after();
+#pragma unroll
+      for (int kk = 0; kk < BT / 16; ++kk) {
+        const uint64_t da = sdesc(ps + uint32_t(kk) * 32, 16, 1024);
+        const uint64_t db = sdesc(vs + uint32_t(kk) * 2048, 64 * 128, 1024);
+        umma(tmem + kOCol, da, db, ID_O, (o_live || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(bar_o);
+    }
+    o_live = true;
+    // The tiles and P are rewritten next: wait for this tile's products.
+    wait_bar(bar_o, uint32_t(it & 1));
+    fence_after();
+  }
+
+  // ---- epilogue: warps 0-3 read their O rows (warp-collective loads; rows
+  // past the chunk load and drop) ------------------------------------------------------
+  if (row_owner) {
+    __syncwarp();
+    const bool live = gr < nrows;
+    const int pos = gr / G, head = kvh * G + gr % G;
+    const int64_t orows = int64_t(p.qlen) * G * gridDim.y;
+    float *rec = p.partials + (int64_t(z) * orows + int64_t(head) * p.qlen + pos) * (D + 2);
+    uint16_t *row = static_cast<uint16_t *>(p.out) + (int64_t(head) * p.qlen + pos) * D;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      float o[32];
+      if (o_live) {
+        tmem_ld32(tmem + lane_base + kOCol + c, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = 0.f;
+      }
+      if (!live) continue;
+      if (p.splits > 1) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4 *>(rec + c + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 v;
+          v.x = E::pack2(__fdiv_rn(o[j], l), __fdiv_rn(o[j + 1], l));
+          v.y = E::pack2(__fdiv_rn(o[j + 2], l), __fdiv_rn(o[j + 3], l));
+          v.z = E::pack2(__fdiv_rn(o[j + 4], l), __fdiv_rn(o[j + 5], l));
+          v.w = E::pack2(__fdiv_rn(o[j + 6], l), __fdiv_rn(o[j + 7], l));
+          *reinterpret_cast<uint4 *>(row + c + j) = v;
+        }
+      }
+    }
+    // A row that saw no token in this split records m = -inf (weight 0).
+    if (live && p.splits > 1) *reinterpret_cast<float2 *>(rec + D) = make_float2(l > 0.f ? m : -INFINITY, l);
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace tc
+
 bool al(const void *ptr, int b) { return (reinterpret_cast<uintptr_t>(ptr) % b) == 0; }
 
 int validate(const ckv_prefill_args &a) {
@@ -523,6 +918,8 @@ Plan make_plan(const ckv_prefill_args &a) {
   return pl;
 }
 
+Params make_params(const ckv_prefill_args &a, const Plan &pl, void *workspace);
+
 template <int BITS, int D, int DT>
 int launch(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
   using C = Cfg<D>;
@@ -536,6 +933,16 @@ int launch(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStrea
     CKV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured[dev].store(1, std::memory_order_release);
   }
+  const Params p = make_params(a, pl, workspace);
+  const dim3 grid(unsigned(pl.tiles), unsigned(a.heads_kv), unsigned(pl.splits));
+  kern<<<grid, kThreads, C::SMEM, st>>>(p);
+  CKV_CUDA_TRY(cudaGetLastError());
+  if (pl.splits == 1) return CKV_OK;
+  return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, a.seq.out,
+                              reinterpret_cast<ckv_stream_t>(st));
+}
+
+Params make_params(const ckv_prefill_args &a, const Plan &pl, void *workspace) {
   const ckv_seq &s = a.seq;
   Params p;
   p.q = s.query;
@@ -567,18 +974,45 @@ int launch(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStrea
   p.scale_log2 = float(double(a.scale) * 1.4426950408889634);
   p.splits = pl.splits;
   p.partials = static_cast<float *>(workspace);
+  return p;
+}
+
+// The tcgen05 kernel for D = 128 and 256 when `use_tc`; D = 64 stays on mma.sync.
+template <int BITS, int D, int DT>
+int launch_tc(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
+  using T = tc::TCfg<D>;
+  auto kern = tc::prefill_tc_kernel<BITS, D, DT>;
+  static std::atomic<int> configured[64];
+  int dev = 0;
+  CKV_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CKV_ERR_INVALID;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    CKV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM));
+    configured[dev].store(1, std::memory_order_release);
+  }
+  const Params p = make_params(a, pl, workspace);
   const dim3 grid(unsigned(pl.tiles), unsigned(a.heads_kv), unsigned(pl.splits));
-  kern<<<grid, kThreads, C::SMEM, st>>>(p);
+  kern<<<grid, kThreads, T::SMEM, st>>>(p);
   CKV_CUDA_TRY(cudaGetLastError());
   if (pl.splits == 1) return CKV_OK;
-  return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, s.out,
+  return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, a.seq.out,
                               reinterpret_cast<ckv_stream_t>(st));
+}
+
+std::atomic<int> g_use_tc{0};
+
+template <int BITS, int D, int DT>
+int launch_any(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
+  if constexpr (D >= 128) {
+    if (g_use_tc.load(std::memory_order_relaxed)) return launch_tc<BITS, D, DT>(a, pl, workspace, st);
+  }
+  return launch<BITS, D, DT>(a, pl, workspace, st);
 }
 
 template <int BITS, int D>
 int dispatch_dt(const ckv_prefill_args &a, const Plan &pl, void *ws, cudaStream_t st) {
-  return a.dtype == CKV_BF16 ? launch<BITS, D, CKV_BF16>(a, pl, ws, st)
-                             : launch<BITS, D, CKV_F16>(a, pl, ws, st);
+  return a.dtype == CKV_BF16 ? launch_any<BITS, D, CKV_BF16>(a, pl, ws, st)
+                             : launch_any<BITS, D, CKV_F16>(a, pl, ws, st);
 }
 
 template <int BITS>
@@ -614,4 +1048,23 @@ extern "C" int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   return args->bits == 8 ? dispatch_d<8>(*args, pl, workspace, st)
                          : dispatch_d<4>(*args, pl, workspace, st);
+}
+
+extern "C" int ckv_prefill_error(int *flag, ckv_stream_t stream) {
+  if (!flag) return CKV_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  unsigned v = 0;
+  CKV_CUDA_TRY(cudaMemcpyFromSymbolAsync(&v, ckv::prefill::tc::g_error, sizeof(v), 0,
+                                         cudaMemcpyDeviceToHost, st));
+  const unsigned zero = 0;
+  CKV_CUDA_TRY(cudaMemcpyToSymbolAsync(ckv::prefill::tc::g_error, &zero, sizeof(zero), 0,
+                                       cudaMemcpyHostToDevice, st));
+  CKV_CUDA_TRY(cudaStreamSynchronize(st));
+  *flag = int(v);
+  return CKV_OK;
+}
+
+extern "C" int ckv_prefill_set_tensor_cores(int on) {
+  ckv::prefill::g_use_tc.store(on ? 1 : 0);
+  return CKV_OK;
 }
