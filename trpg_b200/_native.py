@@ -65,6 +65,13 @@ def load() -> None:
     torch.ops.load_library(str(TORCH_LIB_PATH))
     _loaded = True
     set_dequant(os.environ.get('TRPG_CKV_DEQUANT', 'exact'))
+    set_prefill_tensor_cores(os.environ.get('TRPG_CKV_PREFILL_TC', '0') == '1')
+
+
+def set_prefill_tensor_cores(on: bool) -> None:
+    """Packed prefill at head_dim 128 / 256 on the tcgen05 kernel (True) or
+    the mma.sync kernel (False); process-wide."""
+    library().ckv_prefill_set_tensor_cores(1 if on else 0)
 
 
 def set_dequant(mode: str) -> str:

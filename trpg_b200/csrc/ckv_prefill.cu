@@ -820,20 +820,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         for (int j = 0; j < 32; ++j) o[j] = 0.f;
       }
       if (!live) continue;
+      // Records are D + 2 floats apart (8-byte aligned) and `out` is only
+      // required to be 4-byte aligned: pairs, not wider stores.
       if (p.splits > 1) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4 *>(rec + c + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+        for (int j = 0; j < 32; j += 2)
+          *reinterpret_cast<float2 *>(rec + c + j) = make_float2(o[j], o[j + 1]);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 v;
-          v.x = E::pack2(__fdiv_rn(o[j], l), __fdiv_rn(o[j + 1], l));
-          v.y = E::pack2(__fdiv_rn(o[j + 2], l), __fdiv_rn(o[j + 3], l));
-          v.z = E::pack2(__fdiv_rn(o[j + 4], l), __fdiv_rn(o[j + 5], l));
-          v.w = E::pack2(__fdiv_rn(o[j + 6], l), __fdiv_rn(o[j + 7], l));
-          *reinterpret_cast<uint4 *>(row + c + j) = v;
-        }
+        for (int j = 0; j < 32; j += 2)
+          *reinterpret_cast<uint32_t *>(row + c + j) = E::pack2(__fdiv_rn(o[j], l), __fdiv_rn(o[j + 1], l));
       }
     }
     // A row that saw no token in this split records m = -inf (weight 0).
