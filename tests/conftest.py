@@ -22,3 +22,22 @@ def both_rules(request):
     old = K.set_dequant(request.param)
     yield request.param
     K.set_dequant(old)
+
+
+@pytest.fixture(params=['tcgen05', 'mma_sync'])
+def both_prefill_kernels(request):
+    """Run a packed-prefill test on each kernel for head_dim 128 / 256
+    (``trpg_b200._native.set_prefill_tensor_cores``); the tcgen05 run also
+    checks that no bounded wait of the kernel gave up."""
+    import ctypes
+    import torch
+    from trpg_b200 import _native
+    _native.load()
+    old = _native.prefill_tensor_cores()
+    _native.set_prefill_tensor_cores(request.param == 'tcgen05')
+    yield request.param
+    _native.set_prefill_tensor_cores(old)
+    flag = ctypes.c_int(0)
+    assert _native.library().ckv_prefill_error(ctypes.byref(flag), None) == 0
+    torch.cuda.synchronize()
+    assert flag.value == 0, 'a tcgen05 prefill wait gave up'

@@ -1,5 +1,6 @@
 """Packed prefill parity on the GPU: ``compressed_kv_prefill`` (the B200
-``ckv_prefill`` kernel) against the oracle's dequantize + cat + lower-right
+``ckv_prefill`` kernels: tcgen05 and mma.sync for head_dim 128 / 256) against
+the oracle's dequantize + cat + lower-right
 causal softmax attention, on the reference's own cases
 (tests/test_compressed_prefill_attention.py:26-53) and the edges around them.
 """
@@ -10,7 +11,7 @@ import torch
 from oracle import ckv_oracle as O
 from tests._util import gpu_cache_state, max_abs, to_torch
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures('both_prefill_kernels')]
 # Reference test tolerance (tests/test_compressed_prefill_attention.py:49)
 # and the acceptance bound, max-abs 2e-2 against dequantize + SDPA.
 RTOL, ATOL, MAX_ABS = .03, .004, 2e-2

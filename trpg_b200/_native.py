@@ -65,13 +65,22 @@ def load() -> None:
     torch.ops.load_library(str(TORCH_LIB_PATH))
     _loaded = True
     set_dequant(os.environ.get('TRPG_CKV_DEQUANT', 'exact'))
-    set_prefill_tensor_cores(os.environ.get('TRPG_CKV_PREFILL_TC', '0') == '1')
+    set_prefill_tensor_cores(os.environ.get('TRPG_CKV_PREFILL_TC', '1') == '1')
+
+
+_prefill_tc = True
 
 
 def set_prefill_tensor_cores(on: bool) -> None:
     """Packed prefill at head_dim 128 / 256 on the tcgen05 kernel (True) or
     the mma.sync kernel (False); process-wide."""
+    global _prefill_tc
     library().ckv_prefill_set_tensor_cores(1 if on else 0)
+    _prefill_tc = bool(on)
+
+
+def prefill_tensor_cores() -> bool:
+    return _prefill_tc
 
 
 def set_dequant(mode: str) -> str:

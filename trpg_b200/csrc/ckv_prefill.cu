@@ -995,7 +995,7 @@ int launch_tc(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaSt
                               reinterpret_cast<ckv_stream_t>(st));
 }
 
-std::atomic<int> g_use_tc{0};
+std::atomic<int> g_use_tc{1};   // tcgen05 by default
 
 template <int BITS, int D, int DT>
 int launch_any(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
