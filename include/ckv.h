@@ -291,10 +291,12 @@ int ckv_prefill(const ckv_prefill_args *args, void *workspace, size_t workspace_
  * its tensor-core products since the last call (its outputs are then not
  * valid); read and cleared on `stream`, which it synchronises. */
 int ckv_prefill_error(int *flag, ckv_stream_t stream);
-/* Selects the prefill kernel for head_dim 128 / 256 (process-wide): 1 (the
- * default) the tcgen05 kernel (operands in shared memory, accumulators in
- * tensor memory), 0 the mma.sync kernel.  Same results up to fp32 summation
- * order. */
+/* Selects the prefill kernel for head_dim 128 / 256 (process-wide): 2 (the
+ * default) the pipelined tcgen05 kernel (operands in shared memory,
+ * accumulators in tensor memory; producer warps dequantize the next tile
+ * while the products and the softmax of this one run), 1 the tcgen05 kernel
+ * with its phases in order, 0 the mma.sync kernel.  Same results up to fp32
+ * summation order.  Returns CKV_ERR_INVALID for another value. */
 int ckv_prefill_set_tensor_cores(int on);
 
 /* ---------------------------------------------------------------------- */

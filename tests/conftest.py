@@ -24,17 +24,20 @@ def both_rules(request):
     K.set_dequant(old)
 
 
-@pytest.fixture(params=['tcgen05', 'mma_sync'])
+PREFILL_KERNELS = {'tcgen05_pipelined': 2, 'tcgen05': 1, 'mma_sync': 0}
+
+
+@pytest.fixture(params=list(PREFILL_KERNELS))
 def both_prefill_kernels(request):
     """Run a packed-prefill test on each kernel for head_dim 128 / 256
-    (``trpg_b200._native.set_prefill_tensor_cores``); the tcgen05 run also
-    checks that no bounded wait of the kernel gave up."""
+    (``trpg_b200._native.set_prefill_tensor_cores``); afterwards no bounded
+    wait of a tcgen05 kernel may have given up."""
     import ctypes
     import torch
     from trpg_b200 import _native
     _native.load()
     old = _native.prefill_tensor_cores()
-    _native.set_prefill_tensor_cores(request.param == 'tcgen05')
+    _native.set_prefill_tensor_cores(PREFILL_KERNELS[request.param])
     yield request.param
     _native.set_prefill_tensor_cores(old)
     flag = ctypes.c_int(0)

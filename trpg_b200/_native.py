@@ -65,21 +65,24 @@ def load() -> None:
     torch.ops.load_library(str(TORCH_LIB_PATH))
     _loaded = True
     set_dequant(os.environ.get('TRPG_CKV_DEQUANT', 'exact'))
-    set_prefill_tensor_cores(os.environ.get('TRPG_CKV_PREFILL_TC', '1') == '1')
+    set_prefill_tensor_cores(int(os.environ.get('TRPG_CKV_PREFILL_TC', '2')))
 
 
-_prefill_tc = True
+_prefill_tc = 2
 
 
-def set_prefill_tensor_cores(on: bool) -> None:
-    """Packed prefill at head_dim 128 / 256 on the tcgen05 kernel (True) or
-    the mma.sync kernel (False); process-wide."""
+def set_prefill_tensor_cores(mode: int) -> None:
+    """Packed-prefill kernel at head_dim 128 / 256, process-wide: 0 mma.sync,
+    1 tcgen05 with its phases in order, 2 tcgen05 pipelined (producer warps
+    dequantize ahead, two logit buffers)."""
     global _prefill_tc
-    library().ckv_prefill_set_tensor_cores(1 if on else 0)
-    _prefill_tc = bool(on)
+    mode = int(mode)
+    if library().ckv_prefill_set_tensor_cores(mode) != 0:
+        raise ValueError(f'prefill kernel mode must be 0, 1 or 2, not {mode}')
+    _prefill_tc = mode
 
 
-def prefill_tensor_cores() -> bool:
+def prefill_tensor_cores() -> int:
     return _prefill_tc
 
 

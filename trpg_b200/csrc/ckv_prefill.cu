@@ -844,6 +844,350 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   }
 }
 
+// ---- pipelined variant -----------------------------------------------------------
+// Warps 4-7 produce (dequantize the next tiles into a second K/V buffer);
+// warps 0-3 run the softmax; thread 0 issues the products.  Two S buffers
+// let S(t + 1) run on the tensor cores while the softmax of tile t runs, and
+// P.V of tile t runs while the softmax of tile t + 1 starts.  K and V of a
+// buffer are released separately (K when S of that tile completes, V when
+// P.V does), so the producers refill K early.
+//
+// mbarriers (phase of tile t in buffer b = t & 1 is (t >> 1) & 1):
+//   full_k[b], full_v[b]   producers -> issuer (128 arrivals)
+//   s_done[b]              S(t) complete: softmax may load it; K[b] free
+//   o_done[b]              P.V(t) complete: V[b] and P free, O stable
+constexpr int kProducers = 128;
+
+template <int D>
+struct TCfg2 {
+  static constexpr int BT = 64;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = D * BT * 2;
+  static constexpr int P_BYTES = BM * BT * 2;
+  static constexpr int OFF_Q = 0, OFF_KV = Q_BYTES;             // K0 V0 K1 V1
+  static constexpr int OFF_P = OFF_KV + 4 * KV_BYTES;
+  static constexpr int SMEM = OFF_P + P_BYTES + 1024;
+  static constexpr int K_TASKS = D * (BT / 16) / kProducers;    // (channel, 16 tokens)
+  static constexpr int V_TASKS = BT * (D / 16) / kProducers;    // (token, 16 channels)
+  static_assert(K_TASKS * kProducers == D * (BT / 16), "K tile split");
+  static_assert(V_TASKS * kProducers == BT * (D / 16), "V tile split");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+template <int BITS, int D>
+struct ProdRegs {
+  uint4 k[TCfg2<D>::K_TASKS];
+  float2 km[TCfg2<D>::K_TASKS];
+  uint4 v[TCfg2<D>::V_TASKS];
+  float2 vm[TCfg2<D>::V_TASKS];
+};
+
+template <int BITS, int D>
+__device__ __forceinline__ void read_packed2(const Params &p, int kvh, int t0, int ptid, ProdRegs<BITS, D> &r) {
+  using C = TCfg2<D>;
+  constexpr int SB = C::BT / 16;
+  const int unit = t0 >> 7, s_off = t0 & 127;
+  const uint8_t *kd = p.kd + kvh * p.kds_h + int64_t(unit) * p.kds_u;
+  const float *km = p.km + kvh * p.kms_h + int64_t(unit) * p.kms_u;
+#pragma unroll
+  for (int j = 0; j < C::K_TASKS; ++j) {
+    const int i = ptid + j * kProducers, d = i / SB, s0 = s_off + (i % SB) * 16;
+    if constexpr (BITS == 8) {
+      r.k[j] = __ldg(reinterpret_cast<const uint4 *>(kd + d * 128 + s0));
+    } else {
+      const uint2 x = __ldg(reinterpret_cast<const uint2 *>(kd + d * 64 + s0 / 2));
+      r.k[j] = make_uint4(x.x, x.y, 0u, 0u);
+    }
+    r.km[j] = __ldg(reinterpret_cast<const float2 *>(km + d * 2));
+  }
+  constexpr int CH = D / 16;
+#pragma unroll
+  for (int j = 0; j < C::V_TASKS; ++j) {
+    const int i = ptid + j * kProducers, t = t0 + i / CH, c0 = (i % CH) * 16;
+    const uint8_t *vd = p.vd + kvh * p.vds_h + int64_t(t) * p.vds_t;
+    if constexpr (BITS == 8) {
+      r.v[j] = __ldg(reinterpret_cast<const uint4 *>(vd + (c0 >> 6) * 64 + (c0 & 63)));
+    } else {
+      const uint2 x = __ldg(reinterpret_cast<const uint2 *>(vd + (c0 >> 6) * 32 + (c0 & 63) / 2));
+      r.v[j] = make_uint4(x.x, x.y, 0u, 0u);
+    }
+    r.vm[j] = __ldg(reinterpret_cast<const float2 *>(p.vm + kvh * p.vms_h + int64_t(t) * p.vms_t +
+                                                     (c0 >> 6) * 2));
+  }
+}
+
+template <int BITS, int D, int DT>
+__device__ __forceinline__ void write_k2(const ProdRegs<BITS, D> &r, uint32_t ks, int ptid) {
+  constexpr int SB = TCfg2<D>::BT / 16;
+#pragma unroll
+  for (int j = 0; j < TCfg2<D>::K_TASKS; ++j) {
+    const int i = ptid + j * kProducers, d = i / SB, c = (i % SB) * 2;
+    uint4 lo, hi;
+    dequant16<BITS, DT>(r.k[j], r.km[j].x, r.km[j].y, lo, hi);
+    sts128(ks + swz128(d, c), lo);
+    sts128(ks + swz128(d, c + 1), hi);
+  }
+}
+template <int BITS, int D, int DT>
+__device__ __forceinline__ void write_v2(const ProdRegs<BITS, D> &r, uint32_t vs, int ptid) {
+  constexpr int CH = D / 16;
+#pragma unroll
+  for (int j = 0; j < TCfg2<D>::V_TASKS; ++j) {
+    const int i = ptid + j * kProducers, t = i / CH, c0 = (i % CH) * 16;
+    uint4 lo, hi;
+    dequant16<BITS, DT>(r.v[j], r.vm[j].x, r.vm[j].y, lo, hi);
+    const uint32_t blk = vs + uint32_t(c0 >> 6) * (64 * 128);
+    const int c = (c0 & 63) >> 3;
+    sts128(blk + swz128(t, c), lo);
+    sts128(blk + swz128(t, c + 1), hi);
+  }
+}
+// Window rows [t0, t0 + 64) of K (K-major) or V (MN-major), zero past R.
+template <int D>
+__device__ __forceinline__ void write_resid2(const void *src, int64_t sh, int64_t st, int kvh, int t0,
+                                             int resid, int ptid, uint32_t dst) {
+  constexpr int CH = D / 8;
+  const uint16_t *base = static_cast<const uint16_t *>(src) + kvh * sh;
+  for (int i = ptid; i < 64 * CH; i += kProducers) {
+    const int t = i / CH, c8 = i % CH, tt = t0 + t;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (tt < resid) v = __ldg(reinterpret_cast<const uint4 *>(base + int64_t(tt) * st + c8 * 8));
+    sts128(dst + uint32_t(c8 >> 3) * (64 * 128) + swz128(t, c8 & 7), v);
+  }
+}
+
+template <int BITS, int D, int DT>
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc2_kernel(const __grid_constant__ Params p) {
+  using T = TCfg2<D>;
+  using E = Elem<DT>;
+  constexpr int BT = T::BT;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // full_k[2] full_v[2] s_done[2] o_done[2]
+  __shared__ __align__(8) uint64_t s_bar[8];
+  __shared__ uint32_t s_tmem;
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const uint32_t sb = smem_u32(smem);
+  const uint32_t qs = sb + T::OFF_Q, ps = sb + T::OFF_P;
+  auto kbuf = [&](int b) { return sb + T::OFF_KV + uint32_t(2 * b) * T::KV_BYTES; };
+  auto vbuf = [&](int b) { return sb + T::OFF_KV + uint32_t(2 * b + 1) * T::KV_BYTES; };
+  auto bar = [&](int i) { return smem_u32(&s_bar[i]); };
+  constexpr int FULL_K = 0, FULL_V = 2, S_DONE = 4, O_DONE = 6;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int kvh = blockIdx.y;
+  const int tile = gridDim.x - 1 - blockIdx.x;
+  const int G = p.groups, nrows = p.qlen * G, r0 = tile * BM;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(FULL_K + b), kProducers);
+      mbar_init(bar(FULL_V + b), kProducers);
+      mbar_init(bar(S_DONE + b), 1);
+      mbar_init(bar(O_DONE + b), 1);
+    }
+    mbar_fence_init();
+  }
+  {
+    constexpr int CH = D / 8;
+    const uint16_t *q = static_cast<const uint16_t *>(p.q);
+    for (int i = tid; i < BM * CH; i += kThreads) {
+      const int r = i / CH, c8 = i % CH, gr = r0 + r;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (gr < nrows) {
+        const int pos = gr / G, h = kvh * G + gr % G;
+        v = __ldg(reinterpret_cast<const uint4 *>(q + h * p.qhs + int64_t(pos) * p.qts + c8 * 8));
+      }
+      sts128(qs + uint32_t(c8 >> 3) * (BM * 128) + swz128(r, c8 & 7), v);
+    }
+  }
+  fence_async_smem();
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = s_tmem;
+
+  const int z = p.splits - 1 - int(blockIdx.z), ntiles = p.packed / BT;
+  const int last_row = min(r0 + BM, nrows) - 1;
+  const int rstop = min(p.resid, p.resid - p.qlen + last_row / G + 1);
+  const int total = ntiles + (rstop + BT - 1) / BT;
+  const int a0 = int(int64_t(total) * z / p.splits), a1 = int(int64_t(total) * (z + 1) / p.splits);
+  const int i0 = min(a0, ntiles), np = min(a1, ntiles) - i0;
+  const int rb = max(a0, ntiles) - ntiles, nr = max(a1, ntiles) - ntiles - rb;
+  const int n_items = np + nr;
+  auto tile_base = [&](int t) { return (rb + t - np) * BT; };   // window tiles
+
+  if (warp >= 4) {
+    // ---- producers ----------------------------------------------------------------
+    const int ptid = tid - 4 * 32;
+    ProdRegs<BITS, D> pr;
+    if (np > 0) read_packed2<BITS, D>(p, kvh, i0 * BT, ptid, pr);
+    for (int t = 0; t < n_items; ++t) {
+      const int b = t & 1;
+      const uint32_t par = uint32_t(((t - 2) >> 1) & 1);
+      if (t >= 2) wait_bar(bar(S_DONE + b), par);            // S(t - 2) read K[b]
+      if (t < np) write_k2<BITS, D, DT>(pr, kbuf(b), ptid);
+      else write_resid2<D>(p.rk, p.rks_h, p.rks_t, kvh, tile_base(t), p.resid, ptid, kbuf(b));
+      fence_async_smem();
+      mbar_arrive(bar(FULL_K + b));
+      if (t >= 2) wait_bar(bar(O_DONE + b), par);            // P.V(t - 2) read V[b]
+      if (t < np) write_v2<BITS, D, DT>(pr, vbuf(b), ptid);
+      else write_resid2<D>(p.rv, p.rvs_h, p.rvs_t, kvh, tile_base(t), p.resid, ptid, vbuf(b));
+      fence_async_smem();
+      mbar_arrive(bar(FULL_V + b));
+      if (t + 1 < np) read_packed2<BITS, D>(p, kvh, (i0 + t + 1) * BT, ptid, pr);
+    }
+  } else {
+    // ---- softmax warps (thread tid owns query row tid); thread 0 issues ------------
+    const int gr = r0 + tid;
+    const int vis = p.resid - p.qlen + gr / G;
+    float m = -INFINITY, l = 0.f;
+    const uint32_t lane_base = uint32_t(32 * warp) << 16;
+    constexpr uint32_t ID_S_PACKED = idesc<DT>(BM, BT, 0, 1);
+    constexpr uint32_t ID_S_RESID = idesc<DT>(BM, BT, 0, 0);
+    constexpr uint32_t ID_O = idesc<DT>(BM, D, 0, 1);
+    auto issue_s = [&](int t) {
+      const int b = t & 1;
+      wait_bar(bar(FULL_K + b), uint32_t((t >> 1) & 1));
+      fence_after();
+      const uint32_t ks = kbuf(b);
+      const bool packed = t < np;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint64_t da = sdesc(qs + uint32_t(kk >> 2) * (BM * 128) + uint32_t(kk & 3) * 32, 16, 1024);
+        const uint64_t db = packed ? sdesc(ks + uint32_t(kk) * 2048, T::KV_BYTES, 1024)
+                                   : sdesc(ks + uint32_t(kk >> 2) * (64 * 128) + uint32_t(kk & 3) * 32, 16, 1024);
+        umma(tmem + uint32_t(b * BT), da, db, packed ? ID_S_PACKED : ID_S_RESID, kk > 0);
+      }
+      umma_commit(bar(S_DONE + b));
+    };
+    if (tid == 0 && n_items > 0) issue_s(0);
+    for (int t = 0; t < n_items; ++t) {
+      const int b = t & 1;
+      const bool packed = t < np;
+      const int tbase = packed ? 0 : tile_base(t);
+      wait_bar(bar(S_DONE + b), uint32_t((t >> 1) & 1));
+      __syncwarp();
+      fence_after();
+      float s[BT];
+      {
+        float h[32];
+        tmem_ld32(tmem + lane_base + uint32_t(b * BT), h);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s[j] = h[j];
+        tmem_ld32(tmem + lane_base + uint32_t(b * BT) + 32, h);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s[32 + j] = h[j];
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < BT; ++j) {
+        float x = s[j] * p.scale_log2;
+        if (!packed) {
+          const int tt = tbase + j;
+          if (tt >= p.resid || tt > vis) x = -INFINITY;
+        }
+        s[j] = x;
+        mx = fmaxf(mx, x);
+      }
+      float nm = fmaxf(m, mx);
+      if (nm == -INFINITY) nm = 0.f;
+      const float alpha = ex2(m - nm);
+      m = nm;
+      float rs = 0.f;
+      uint32_t w[BT / 2];
+#pragma unroll
+      for (int k = 0; k < BT / 2; ++k) {
+        const float e0 = ex2(s[2 * k] - m), e1 = ex2(s[2 * k + 1] - m);
+        rs += e0 + e1;
+        w[k] = E::pack2(e0, e1);
+      }
+      l = l * alpha + rs;
+      // S of the next tile runs on the tensor cores while this one finishes.
+      if (tid == 0 && t + 1 < n_items) issue_s(t + 1);
+      if (t >= 1) {
+        // P.V(t - 1) must be complete: it reads P, and O is rescaled below.
+        wait_bar(bar(O_DONE + ((t - 1) & 1)), uint32_t(((t - 1) >> 1) & 1));
+        __syncwarp();
+        fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 32) {
+            float o[32];
+            tmem_ld32(tmem + lane_base + kOCol + c, o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= alpha;
+            tmem_st32(tmem + lane_base + kOCol + c, o);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < BT / 8; ++c)
+        sts128(ps + swz128(tid, c), make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]));
+      fence_async_smem();
+      fence_before();
+      named_sync(1, 4 * 32);
+      if (tid == 0) {
+        wait_bar(bar(FULL_V + b), uint32_t((t >> 1) & 1));
+        fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BT / 16; ++kk) {
+          const uint64_t da = sdesc(ps + uint32_t(kk) * 32, 16, 1024);
+          const uint64_t db = sdesc(vbuf(b) + uint32_t(kk) * 2048, 64 * 128, 1024);
+          umma(tmem + kOCol, da, db, ID_O, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(O_DONE + b));
+      }
+    }
+    // ---- epilogue --------------------------------------------------------------------
+    const bool o_live = n_items > 0;
+    if (o_live) {
+      const int t = n_items - 1;
+      wait_bar(bar(O_DONE + (t & 1)), uint32_t((t >> 1) & 1));
+    }
+    __syncwarp();
+    fence_after();
+    const bool live = gr < nrows;
+    const int pos = gr / G, head = kvh * G + gr % G;
+    const int64_t orows = int64_t(p.qlen) * G * gridDim.y;
+    float *rec = p.partials + (int64_t(z) * orows + int64_t(head) * p.qlen + pos) * (D + 2);
+    uint16_t *row = static_cast<uint16_t *>(p.out) + (int64_t(head) * p.qlen + pos) * D;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+      float o[32];
+      if (o_live) {
+        tmem_ld32(tmem + lane_base + kOCol + c, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = 0.f;
+      }
+      if (!live) continue;
+      if (p.splits > 1) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          *reinterpret_cast<float2 *>(rec + c + j) = make_float2(o[j], o[j + 1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          *reinterpret_cast<uint32_t *>(row + c + j) = E::pack2(__fdiv_rn(o[j], l), __fdiv_rn(o[j + 1], l));
+      }
+    }
+    if (live && p.splits > 1) *reinterpret_cast<float2 *>(rec + D) = make_float2(l > 0.f ? m : -INFINITY, l);
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 }  // namespace tc
 
 bool al(const void *ptr, int b) { return (reinterpret_cast<uintptr_t>(ptr) % b) == 0; }
@@ -995,12 +1339,36 @@ int launch_tc(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaSt
                               reinterpret_cast<ckv_stream_t>(st));
 }
 
-std::atomic<int> g_use_tc{1};   // tcgen05 by default
+template <int BITS, int D, int DT>
+int launch_tc2(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
+  using T = tc::TCfg2<D>;
+  auto kern = tc::prefill_tc2_kernel<BITS, D, DT>;
+  static std::atomic<int> configured[64];
+  int dev = 0;
+  CKV_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return CKV_ERR_INVALID;
+  if (!configured[dev].load(std::memory_order_acquire)) {
+    CKV_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM));
+    configured[dev].store(1, std::memory_order_release);
+  }
+  const Params p = make_params(a, pl, workspace);
+  const dim3 grid(unsigned(pl.tiles), unsigned(a.heads_kv), unsigned(pl.splits));
+  kern<<<grid, kThreads, T::SMEM, st>>>(p);
+  CKV_CUDA_TRY(cudaGetLastError());
+  if (pl.splits == 1) return CKV_OK;
+  return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, a.seq.out,
+                              reinterpret_cast<ckv_stream_t>(st));
+}
+
+// 0: mma.sync; 1: tcgen05, phases in order; 2: tcgen05, pipelined.
+std::atomic<int> g_use_tc{2};
 
 template <int BITS, int D, int DT>
 int launch_any(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaStream_t st) {
   if constexpr (D >= 128) {
-    if (g_use_tc.load(std::memory_order_relaxed)) return launch_tc<BITS, D, DT>(a, pl, workspace, st);
+    const int mode = g_use_tc.load(std::memory_order_relaxed);
+    if (mode == 2) return launch_tc2<BITS, D, DT>(a, pl, workspace, st);
+    if (mode == 1) return launch_tc<BITS, D, DT>(a, pl, workspace, st);
   }
   return launch<BITS, D, DT>(a, pl, workspace, st);
 }
@@ -1061,6 +1429,7 @@ extern "C" int ckv_prefill_error(int *flag, ckv_stream_t stream) {
 }
 
 extern "C" int ckv_prefill_set_tensor_cores(int on) {
-  ckv::prefill::g_use_tc.store(on ? 1 : 0);
+  if (on < 0 || on > 2) return CKV_ERR_INVALID;
+  ckv::prefill::g_use_tc.store(on);
   return CKV_OK;
 }
