@@ -117,8 +117,9 @@ def test_install_routes_the_reference_prefill_kernel_module():
 
 
 def test_patch_prefill_limits():
-    """Prefill routing limits of the attention patch: 1024 tokens by default,
-    4096 with ``prefill=True``, none with ``prefill=False``."""
+    """Prefill routing limits of the attention patch: by default 1024 tokens
+    at head_dim 64 and 4096 at head_dim 256, 4096 with ``prefill=True``,
+    none with ``prefill=False``."""
     from transformers import Qwen3_5TextConfig
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     from trpg_b200.compressed_kv_attention import compressed_kv_info, configure_compressed_kv_attention
@@ -135,3 +136,9 @@ def test_patch_prefill_limits():
         limits.append(module._direct_kv_prefill_max)
     assert limits == [1024, 4096, 0]
     assert compressed_kv_info(module)['direct_prefill_calls'] == 0
+    wide = Qwen3_5Attention(Qwen3_5TextConfig(hidden_size=128, intermediate_size=256,
+                                              num_hidden_layers=1, num_attention_heads=4,
+                                              num_key_value_heads=2, head_dim=256,
+                                              layer_types=['full_attention']), 0)
+    configure_compressed_kv_attention(wide)
+    assert wide._direct_kv_prefill_max == 4096

@@ -15,10 +15,11 @@ Mirror of ``models/compressed_kv_attention.py`` over the B200 kernels:
   ``mtp_verification_scope`` (``trpg_b200.mtp_verification_kernels``, which
   shares the reference's flag once ``trpg_b200.install`` has run), and
   chunks over a packed history to ``compressed_kv_prefill``
-  (``trpg_b200.compressed_prefill_attention``): 16..1024 tokens by default,
-  where the packed kernel is faster than dequantize + SDPA, up to 4096 with
-  ``prefill=True``, none with ``prefill=False``.  The reference only exposes
-  that kernel as a standalone API.
+  (``trpg_b200.compressed_prefill_attention``) where the packed kernel is
+  faster than dequantize + SDPA: by default 16..4096 tokens at head_dim 128
+  and 256 (the tcgen05 kernel) and 16..1024 at head_dim 64 (the mma.sync
+  kernel); 16..4096 with ``prefill=True``, none with ``prefill=False``.  The
+  reference only exposes that kernel as a standalone API.
 
 Kernel launch errors raise; only "unsupported" returns ``None``.
 """
@@ -169,8 +170,10 @@ def configure_compressed_kv_attention(model, enabled=True, prefill=None):
     """Patch every ``Qwen3_5Attention`` (reference ``:85-95``).
 
     Prefill chunks over a packed history go to the packed prefill kernel
-    instead of dequantize + SDPA: 16..1024 tokens by default (``prefill=None``),
-    16..4096 with ``prefill=True``, none with ``prefill=False``.
+    instead of dequantize + SDPA: by default (``prefill=None``) 16..4096
+    tokens at head_dim 128 / 256 and 16..1024 at head_dim 64, where each
+    kernel is the faster; 16..4096 with ``prefill=True``, none with
+    ``prefill=False``.
     """
     from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Attention
     for module in model.modules():
@@ -182,7 +185,8 @@ def configure_compressed_kv_attention(model, enabled=True, prefill=None):
             module._direct_kv_verify_calls = module._direct_kv_prefill_calls = 0
             module.forward = MethodType(_forward, module)
         module._direct_kv_enabled = bool(enabled)
-        module._direct_kv_prefill_max = 1024 if prefill is None else (4096 if prefill else 0)
+        default = 4096 if getattr(module, 'head_dim', 0) >= 128 else 1024
+        module._direct_kv_prefill_max = default if prefill is None else (4096 if prefill else 0)
     return compressed_kv_info(model)
 
 
