@@ -309,19 +309,20 @@ int ckv_prefill_set_tensor_cores(int on);
  * buffer into its address space (CUDA IPC over NVLink, plain peer mappings,
  * no multicast), and one launch per rank and step
  *   1. writes this rank's partial (rows x (D+2) fp32, as ckv_attention with
- *      partial = 1 leaves it) into every rank's buffer, then raises this
- *      rank's flag in every buffer (system-scope release);
- *   2. waits until the flags of all ranks are raised in its own buffer
- *      (system-scope acquire; bounded: after `spin_limit` clock cycles, or
- *      2^31 when 0, it sets the buffer's error word and skips step 3);
- *   3. merges the world partials into `out` [rows, D] of `dtype`, with the
- *      rule of ckv_combine_partials (models/compressed_kv_kernels.py:85-89).
+ *      partial = 1 leaves it) into every rank's buffer, each value as one
+ *      8-byte word together with the step number that wrote it;
+ *   2. merges the world partials into `out` [rows, D] of `dtype`, with the
+ *      rule of ckv_combine_partials (models/compressed_kv_kernels.py:85-89),
+ *      reading each word once its step field shows this step (an aligned
+ *      8-byte store is seen whole, so no fence or separate flag is needed);
+ *      the wait is bounded: after `spin_limit` clock cycles (2^31 when 0) it
+ *      sets the buffer's error word and leaves the output unwritten.
  * The step number is a counter in the buffer that each launch advances, so
- * the launch can be captured in a CUDA graph and replayed. Partials and
- * flags alternate between two slots by step parity: a rank's step s + 1
- * waits for every rank's step s + 1 partial, which each rank publishes only
- * after its own step s, so no rank overwrites a slot that another rank is
- * still reading. Every rank must make the same sequence of calls.
+ * the launch can be captured in a CUDA graph and replayed. Partials
+ * alternate between two slots by step parity: a rank's step s + 1 waits for
+ * every rank's step s + 1 partial, which each rank publishes only after its
+ * own step s, so no rank overwrites a slot that another rank is still
+ * reading. Every rank must make the same sequence of calls.
  *
  * Buffer: ckv_exchange_bytes(world, rows, head_dim) bytes, zeroed, from
  * ckv_exchange_alloc; world <= CKV_EXCHANGE_MAX_WORLD.

@@ -70,7 +70,7 @@ def test_cpu_tensors_raise_instead_of_falling_back():
 def test_exchange_sizes_and_arguments_are_checked_on_the_host():
     lib = _native.library()
     rows, d = 16, 256
-    want = 512 + 2 * 2 * rows * (d + 2) * 4
+    want = 256 + 2 * 2 * rows * (d + 2) * 8
     assert lib.ckv_exchange_bytes(2, rows, d) == (want + 255) // 256 * 256
     assert lib.ckv_exchange_bytes(0, rows, d) == 0
     assert lib.ckv_exchange_bytes(9, rows, d) == 0           # above CKV_EXCHANGE_MAX_WORLD
