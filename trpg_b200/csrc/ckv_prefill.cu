@@ -845,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 }
 
 // ---- pipelined variant -----------------------------------------------------------
-// Warps 4-7 produce (dequantize the next tiles into a second K/V buffer);
+// Warps 4-11 produce (dequantize the next tiles into a second K/V buffer);
 // warps 0-3 run the softmax; thread 0 issues the products.  Two S buffers
 // let S(t + 1) run on the tensor cores while the softmax of tile t runs, and
 // P.V of tile t runs while the softmax of tile t + 1 starts.  K and V of a
@@ -853,10 +853,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 // P.V does), so the producers refill K early.
 //
 // mbarriers (phase of tile t in buffer b = t & 1 is (t >> 1) & 1):
-//   full_k[b], full_v[b]   producers -> issuer (128 arrivals)
+//   full_k[b], full_v[b]   producers -> issuer (one arrival per producer)
 //   s_done[b]              S(t) complete: softmax may load it; K[b] free
 //   o_done[b]              P.V(t) complete: V[b] and P free, O stable
-constexpr int kProducers = 128;
+constexpr int kProducers = 256;                    // warps 4-11
+constexpr int kThreads2 = 4 * 32 + kProducers;    // + the softmax warps 0-3
 
 template <int D>
 struct TCfg2 {
@@ -957,7 +958,7 @@ __device__ __forceinline__ void write_resid2(const void *src, int64_t sh, int64_
 }
 
 template <int BITS, int D, int DT>
-__global__ void __launch_bounds__(kThreads, 1) prefill_tc2_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads2, 1) prefill_tc2_kernel(const __grid_constant__ Params p) {
   using T = TCfg2<D>;
   using E = Elem<DT>;
   constexpr int BT = T::BT;
@@ -996,7 +997,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc2_kernel(const __grid_c
   {
     constexpr int CH = D / 8;
     const uint16_t *q = static_cast<const uint16_t *>(p.q);
-    for (int i = tid; i < BM * CH; i += kThreads) {
+    for (int i = tid; i < BM * CH; i += kThreads2) {
       const int r = i / CH, c8 = i % CH, gr = r0 + r;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (gr < nrows) {
@@ -1353,7 +1354,7 @@ int launch_tc2(const ckv_prefill_args &a, const Plan &pl, void *workspace, cudaS
   }
   const Params p = make_params(a, pl, workspace);
   const dim3 grid(unsigned(pl.tiles), unsigned(a.heads_kv), unsigned(pl.splits));
-  kern<<<grid, kThreads, T::SMEM, st>>>(p);
+  kern<<<grid, tc::kThreads2, T::SMEM, st>>>(p);
   CKV_CUDA_TRY(cudaGetLastError());
   if (pl.splits == 1) return CKV_OK;
   return ckv_combine_partials(p.partials, pl.splits, int64_t(a.heads_q) * a.qlen, D, DT, a.seq.out,
