@@ -870,17 +870,28 @@ def measure_extra(w, args, world, rank, device, min_steps=20):
             part0 = fn()[0]
         px = PeerExchange(part0.shape[0], D)
         try:
-            align = lambda: (barrier(world), torch.cuda.synchronize())
-            step_s = graph_seconds(lambda: px.combine(fn()[0], torch.bfloat16), replays=200, align=align)
-            ex_s = graph_seconds(lambda: px.combine(part0, torch.bfloat16), replays=200, align=align)
-            failed = px.error()
+            # One checked exchange first: the merged output must equal the
+            # NCCL path's and no wait may give up, before any timing.
+            with torch.inference_mode():
+                dist.all_gather_into_tensor(gathered, part0)
+                want = combine(gathered.view(world, *part0.shape), torch.bfloat16)
+                got = px.combine(part0, torch.bfloat16)
+            bad = float(px.error() != 0 or not torch.equal(got, want))
+            bad = max_over_ranks(bad, world)
+            if bad:
+                out['peer_exchange'] = {'unavailable': 'the checked exchange disagreed with NCCL or gave up'}
+            else:
+                align = lambda: (barrier(world), torch.cuda.synchronize())
+                step_s = graph_seconds(lambda: px.combine(fn()[0], torch.bfloat16), replays=200, align=align)
+                ex_s = graph_seconds(lambda: px.combine(part0, torch.bfloat16), replays=200, align=align)
+                failed = px.error()
+                step_us = max_over_ranks(step_s * 1e6, world)
+                out['peer_exchange'] = {'us_per_step_max_rank': step_us,
+                                        'us_exchange_combine_max_rank': max_over_ranks(ex_s * 1e6, world),
+                                        'value': tokens / (step_us * 1e-6), 'unit': 'tok/s',
+                                        'wait_gave_up': bool(max_over_ranks(float(failed), world))}
         finally:
             px.close()
-        step_us = max_over_ranks(step_s * 1e6, world)
-        out['peer_exchange'] = {'us_per_step_max_rank': step_us,
-                                'us_exchange_combine_max_rank': max_over_ranks(ex_s * 1e6, world),
-                                'value': tokens / (step_us * 1e-6), 'unit': 'tok/s',
-                                'wait_gave_up': bool(max_over_ranks(float(failed), world))}
     return out
 
 
