@@ -47,8 +47,12 @@ def test_one_long_sequence_is_one_wave():
 
 
 def test_many_pairs_fill_whole_waves_exactly():
-    # 16 x 4 pairs of 130 items: 8 waves of about 7 items, rounded by
-    # largest remainders to exactly 8 x 148 CTAs (not 64 x 19 = 1216).
-    assert _plan([16384] * 16, nq=4) == 8 * SMS
+    # 16 x 4 pairs of 130 items with 16 query rows (32 items a CTA): 2 waves
+    # of about 28 items, rounded by largest remainders to exactly 2 x 148
+    # CTAs (not 64 x 5 = 320).
+    assert _plan([16384] * 16, nq=4) == 2 * SMS
+    # 4 query rows (24 items a CTA): whole waves as well.
     ragged = [1024 + (i * 1777) % 7169 for i in range(64)]
-    assert _plan(ragged) % SMS == 0
+    packed = [(n - 256) // 128 * 128 for n in ragged]
+    total = sum(p // 128 + -(-(n - p) // 64) for n, p in zip(ragged, packed)) * 4
+    assert _plan(ragged) == -(-total // (SMS * 24)) * SMS

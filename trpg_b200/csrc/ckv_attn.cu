@@ -656,7 +656,15 @@ int seq_items(const ckv_seq &s) {
   return (s.unit_end - s.unit_begin) + (s.resid_end - s.resid_begin + RCHUNK - 1) / RCHUNK;
 }
 
-constexpr int kItemsPerCta = 8;   // items (blocks / residual chunks) one CTA pipelines
+// Items (blocks / residual chunks) a CTA of a many-pair launch takes on:
+// each CTA pays a fixed start-up and a record + merge tail, the tail four
+// times larger with 16 query rows than with 4, so the 16-row variant takes
+// longer ranges.  Measured on B200 (kernel time from graph replay):
+//   64 ragged sequences (1024..8192), 4 rows: 8 items 189 us, 16 items 169 us,
+//     24 items 164 us, 32 items 183 us;
+//   16 sequences x 4 queries at 16K, 16 rows: 8 items 223 us, 16 items 187 us,
+//     24 items 186 us, 32 items 173 us, 44 items 173 us.
+int items_per_cta(int rows) { return rows > 8 ? 32 : 24; }
 
 // CTAs per (sequence, KV head): a whole number of waves of one CTA per SM,
 // shared out in proportion to each pair's items.
@@ -664,10 +672,10 @@ int make_plan(const ckv_attn_args &a, int D, Plan &pl) {
   const int sms = sm_count();
   int64_t total = 0;
   for (int i = 0; i < a.num_seqs; ++i) total += int64_t(seq_items(a.seqs[i])) * a.heads_kv;
-  const int64_t per_wave = int64_t(sms) * kItemsPerCta;
+  const int64_t per_wave = int64_t(sms) * items_per_cta(a.nq * (a.heads_q / a.heads_kv));
   // Few pairs (each gets at least 8 CTAs of one wave): one wave, however long
   // the ranges -- no wave tails and fewer records to merge.  Many pairs:
-  // whole waves of about kItemsPerCta items, which the block scheduler
+  // whole waves of about items_per_cta items, which the block scheduler
   // balances across ragged pairs.
   const int64_t pairs = int64_t(a.num_seqs) * a.heads_kv;
   const int64_t waves =
