@@ -3,9 +3,13 @@
 Mirror of ``models/compressed_prefill_kernels.py:98-111``: ``prefill(query,
 view, scale)`` runs after the public eligibility checks of
 ``trpg_b200.compressed_prefill_attention.compressed_kv_prefill`` and reads
-the whole history once per CTA of 128 query rows (``BM`` in
-``csrc/ckv_prefill.cu``: 8 warps of 16 rows, position-major over the G query
-heads of a KV head), never materialising the dequantized history.
+the whole history once per CTA of 128 query rows (position-major over the G
+query heads of a KV head), never materialising the dequantized history.  For
+head_dim 128 and 256 the CTA's products run on tcgen05 (operands staged in
+shared memory by producer warps that dequantize the codes, logits and output
+accumulated in tensor memory); for head_dim 64, and when
+``trpg_b200._native.set_prefill_tensor_cores(0)`` selects it, on mma.sync
+(8 warps of 16 rows, ``BM`` in ``csrc/ckv_prefill.cu``).
 """
 from __future__ import annotations
 
